@@ -1,0 +1,144 @@
+/*
+ * lmce — C ABI of the B200 (sm_100a) fused lm_head cross-entropy head.
+ *
+ * Plain pointers, sizes and a CUDA stream handle; no framework types. Every
+ * call is stream-ordered on `stream` (a cudaStream_t passed as void*), never
+ * synchronises, never aborts, and never allocates device memory: the caller
+ * owns every buffer, including workspaces sized by the *_bytes queries.
+ * Every function returns LMCE_OK or an LMCE_ERR_* code; lmce_last_error()
+ * gives a thread-local message for the last failing call on this thread.
+ * Conditions detected by kernels (a bounded wait that gave up, a label
+ * outside [0, V)) are recorded in a per-device error word read by
+ * lmce_device_error().
+ *
+ * Reference interface replaced (fokyso82002-rgb/rus):
+ *   FusedChunkedLMHeadFn.forward  solution/ops.py:179-330
+ *   FusedChunkedLMHeadFn.backward solution/ops.py:332-339
+ *   lm_head_piece_kernel          solution/kernels.py:453-531
+ *   lm_head_finish_kernel         solution/kernels.py:534-565
+ * The Python autograd wrapper rus_b200.ops.chunked_lm_head binds these with
+ * ctypes and keeps the reference's signature (solution/ops.py:342-349).
+ */
+#ifndef LMCE_H_
+#define LMCE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LMCE_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define LMCE_API __attribute__((visibility("default")))
+#else
+#define LMCE_API
+#endif
+
+enum {
+  LMCE_OK = 0,
+  LMCE_ERR_INVALID_ARGUMENT = 1, /* null pointer, bad size, misaligned buffer */
+  LMCE_ERR_UNSUPPORTED = 2,      /* device is not sm_100, dtype or shape not supported */
+  LMCE_ERR_CUDA = 3,             /* a CUDA runtime/driver call failed */
+  LMCE_ERR_TIMEOUT = 4,          /* a bounded on-device wait gave up (device error word) */
+  LMCE_ERR_LABEL_RANGE = 5,      /* a label was neither -100 nor in [0, V) (device error word) */
+  LMCE_ERR_WORKSPACE = 6         /* workspace too small */
+};
+
+enum { LMCE_DTYPE_F16 = 0, LMCE_DTYPE_BF16 = 1 };
+
+/* Per-token partial softmax statistics, 24 bytes:
+ *   m    running max of the logits (logits rounded to the input dtype)
+ *   s    sum_v exp(z_v - m)
+ *   w    sum_v exp(z_v - m) * (z_v - m)
+ *   best max logit, idx its lowest global vocab id
+ *   zy   target logit, -inf if the target is outside the covered vocab range
+ * The same record is produced by a vocab slab, a vocab shard, or their merge. */
+typedef struct lmce_part {
+  float m, s, w, best;
+  int32_t idx;
+  float zy;
+} lmce_part;
+
+LMCE_API int lmce_abi_version(void);
+LMCE_API const char* lmce_last_error(void);
+
+/* Reads the device error word of the current device (synchronous: waits for
+ * the device). reset != 0 clears it afterwards. Returns LMCE_OK, or the first
+ * LMCE_ERR_* code a kernel recorded. */
+LMCE_API int lmce_device_error(int reset);
+
+/* ---------------------------------------------------------------- forward */
+
+/* Number of per-token partial records lmce_fwd_stats writes for this shape on
+ * the current device (vocab slabs processed by different CTAs). */
+LMCE_API int64_t lmce_fwd_num_parts(int64_t n_tokens, int64_t vocab_local);
+
+/* Fused logits GEMM + online statistics over one vocab shard
+ * (replaces ops.py:216-251 pass 1 and kernels.py:480-516 MODE 0).
+ *   hidden  [n_tokens, hidden_dim]     dtype, row-major, 16-byte aligned rows
+ *   weight  [vocab_local, hidden_dim]  dtype, rows vocab_offset.. of the full head
+ *   labels  [n_tokens] int64, global vocab ids, -100 = ignored
+ *   parts   [n_tokens, n_parts] lmce_part, n_parts = lmce_fwd_num_parts(...)
+ * hidden_dim must be a multiple of 64. No [n_tokens, vocab] buffer is used. */
+LMCE_API int lmce_fwd_stats(const void* hidden, const void* weight, const int64_t* labels, int64_t n_tokens,
+                   int64_t hidden_dim, int64_t vocab_local, int64_t vocab_offset, int dtype, lmce_part* parts,
+                   int64_t n_parts, void* stream);
+
+/* Merges n_parts records per token into one record per token (used before a
+ * cross-GPU gather). Record (token t, part p) is parts[t*tok_stride + p*part_stride]. */
+LMCE_API int lmce_stats_reduce(const lmce_part* parts, int64_t n_parts, int64_t tok_stride, int64_t part_stride,
+                      int64_t n_tokens, lmce_part* record_out, void* stream);
+
+/* Merges the records and finishes the forward (replaces kernels.py:534-565 and
+ * the loss reduction at ops.py:268-277):
+ *   lse = m + ln s;  entropy = ln s - w / s;  nll = lse - z_y (0 when label == -100)
+ *   argmax = lowest vocab id of the max logit
+ *   denom = *num_items_dev if non-null, else num_items if >= 0, else #(label != -100); clamped to >= 1
+ *   loss = sum(nll) / denom  (fixed-order reduction, deterministic)
+ * Outputs: lse, nll, entropy [n_tokens] fp32; argmax [n_tokens] int64; loss, denom fp32 scalars. */
+LMCE_API int lmce_stats_finish(const lmce_part* parts, int64_t n_parts, int64_t tok_stride, int64_t part_stride,
+                      const int64_t* labels, int64_t n_tokens, const float* num_items_dev, double num_items,
+                      float* lse, float* nll, float* entropy, int64_t* argmax, float* loss, float* denom,
+                      void* stream);
+
+/* --------------------------------------------------------------- backward */
+
+/* Workspace bytes for lmce_backward (vocab-chunk gradient tile, compacted
+ * rows, fp32 dX accumulator). v_chunk is rounded up to a multiple of 256. */
+LMCE_API size_t lmce_bwd_workspace_bytes(int64_t n_tokens, int64_t hidden_dim, int64_t vocab_local, int64_t v_chunk);
+
+/* Recomputes the logits per vocab chunk, forms G = (softmax - onehot) in
+ * registers and contracts it into dX and dW (replaces ops.py:280-322 and
+ * ops.py:333-339; dW is new). Only tokens with label != -100 are processed.
+ *   lse        [n_tokens] fp32 from lmce_stats_finish (global over all shards)
+ *   grad_loss  device fp32 scalar d(loss) (nullable: 1.0)
+ *   denom      device fp32 scalar from lmce_stats_finish
+ *   d_hidden     [n_tokens, hidden_dim] dtype  (nullable) receives dX
+ *   d_hidden_f32 [n_tokens, hidden_dim] fp32   (nullable) receives this shard's
+ *                fp32 dX contribution, zero rows for ignored tokens; it must be
+ *                zero-filled by the caller and is meant for a cross-GPU sum
+ *   d_weight   [vocab_local, hidden_dim] dtype (nullable) receives dW */
+LMCE_API int lmce_backward(const void* hidden, const void* weight, const int64_t* labels, const float* lse,
+                  int64_t n_tokens, int64_t hidden_dim, int64_t vocab_local, int64_t vocab_offset, int dtype,
+                  const float* grad_loss, const float* denom, void* d_hidden, float* d_hidden_f32,
+                  void* d_weight, int64_t v_chunk, void* workspace, size_t workspace_bytes, void* stream);
+
+/* d_hidden = dtype(d_hidden_f32), elementwise over n_tokens x hidden_dim. */
+LMCE_API int lmce_dx_finalize(const float* d_hidden_f32, int64_t n_tokens, int64_t hidden_dim, int dtype,
+                     void* d_hidden, void* stream);
+
+/* ------------------------------------------------------------ diagnostics */
+
+/* Launches a kernel whose bounded wait is never satisfied; after timeout_ns it
+ * records LMCE_ERR_TIMEOUT in the device error word and returns normally.
+ * Exercises the failure path without hanging or faulting the GPU. */
+LMCE_API int lmce_selftest_wait_timeout(uint64_t timeout_ns, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LMCE_H_ */

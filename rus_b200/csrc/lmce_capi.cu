@@ -1,0 +1,709 @@
+// C-ABI, launch code and the small auxiliary kernels of the lm_head CE head.
+//
+// Host responsibilities here: argument validation, TMA tensor-map encoding,
+// schedule sizing (vocab slabs, vocab chunks), and stream-ordered launches.
+// Nothing in this file allocates device memory or synchronises the stream.
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/lmce.h"
+#include "lmce_engine.cuh"
+
+using namespace lmce;
+
+static_assert(sizeof(Part) == sizeof(lmce_part), "record layout mismatch");
+
+// Library-wide device error word (one instance per device).
+__device__ int g_lmce_err;
+
+namespace {
+
+thread_local char t_err[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_err, sizeof(t_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+#define LMCE_CUDA(expr)                                                                         \
+  do {                                                                                          \
+    cudaError_t e_ = (expr);                                                                    \
+    if (e_ != cudaSuccess) return fail(LMCE_ERR_CUDA, "%s: %s", #expr, cudaGetErrorString(e_)); \
+  } while (0)
+
+// ------------------------------------------------------------ device info ---
+
+struct DevInfo {
+  int sms = 0;
+  int major = 0, minor = 0;
+  int* err_ptr = nullptr;
+  bool ok = false;
+};
+
+constexpr int kMaxDevices = 64;
+DevInfo g_dev[kMaxDevices];
+std::mutex g_dev_mu;
+
+int device_info(DevInfo** out) {
+  int dev = 0;
+  LMCE_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return fail(LMCE_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  DevInfo& d = g_dev[dev];
+  if (!d.ok) {
+    LMCE_CUDA(cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev));
+    LMCE_CUDA(cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev));
+    LMCE_CUDA(cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev));
+    if (d.major != 10 || d.minor != 0)
+      return fail(LMCE_ERR_UNSUPPORTED, "lmce is built for sm_100a (B200); device %d is sm_%d%d", dev, d.major,
+                  d.minor);
+    void* p = nullptr;
+    LMCE_CUDA(cudaGetSymbolAddress(&p, g_lmce_err));
+    d.err_ptr = static_cast<int*>(p);
+    d.ok = true;
+  }
+  *out = &d;
+  return LMCE_OK;
+}
+
+unsigned long long wait_timeout_ns() {
+  static unsigned long long v = [] {
+    const char* s = std::getenv("LMCE_WAIT_TIMEOUT_MS");
+    unsigned long long ms = s ? std::strtoull(s, nullptr, 10) : 4000ull;
+    if (ms == 0) ms = 4000ull;
+    return ms * 1000000ull;
+  }();
+  return v;
+}
+
+// ------------------------------------------------------------ tensor maps ---
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+int get_encoder() {
+  static std::once_flag once;
+  static int status = LMCE_OK;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* fn = nullptr;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr) {
+      status = fail(LMCE_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+      return;
+    }
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  return g_encode ? LMCE_OK : fail(LMCE_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+}
+
+// Row-major 2-D tensor [outer][inner] of 16-bit elements, 128-byte swizzle, box {64, box_outer}.
+int make_map(CUtensorMap* m, const void* base, bool bf16, uint64_t inner, uint64_t outer, uint64_t ld_elems,
+             uint32_t box_outer) {
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0) return fail(LMCE_ERR_INVALID_ARGUMENT, "tensor base not 16B aligned");
+  if ((ld_elems * 2) % 16 != 0) return fail(LMCE_ERR_INVALID_ARGUMENT, "row stride not a multiple of 16 bytes");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld_elems * 2};
+  cuuint32_t box[2] = {64, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                        const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(LMCE_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return LMCE_OK;
+}
+
+// ---------------------------------------------------------------- engine ---
+
+constexpr int kBN = 256;
+constexpr int kStages = 4;
+
+template <int KIND, bool A_MN, bool B_MN, bool BF16>
+int launch_engine(const CUtensorMap& ma, const CUtensorMap& mb, const EngineParams& p, int grid,
+                  cudaStream_t st) {
+  auto kern = lmce_gemm_kernel<KIND, kBN, A_MN, B_MN, BF16, kStages>;
+  constexpr int smem = engine_smem_bytes<kBN, kStages>();
+  static bool attr_done[kMaxDevices] = {};
+  int dev = 0;
+  LMCE_CUDA(cudaGetDevice(&dev));
+  if (!attr_done[dev]) {
+    LMCE_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr_done[dev] = true;
+  }
+  kern<<<grid, NUM_THREADS, smem, st>>>(ma, mb, p);
+  LMCE_CUDA(cudaGetLastError());
+  return LMCE_OK;
+}
+
+template <int KIND, bool A_MN, bool B_MN>
+int launch_engine_dt(bool bf16, const CUtensorMap& ma, const CUtensorMap& mb, const EngineParams& p, int grid,
+                     cudaStream_t st) {
+  return bf16 ? launch_engine<KIND, A_MN, B_MN, true>(ma, mb, p, grid, st)
+              : launch_engine<KIND, A_MN, B_MN, false>(ma, mb, p, grid, st);
+}
+
+// Vocab slabs per token block: fill the SMs with whole waves of (block, slab)
+// units while keeping slabs of near-equal tile counts.
+int choose_slabs(int num_m, int num_n, int sms) {
+  int best = 1;
+  double best_eff = -1.0;
+  const int smax = num_n < 256 ? num_n : 256;
+  for (int s = 1; s <= smax; ++s) {
+    const long long units = static_cast<long long>(num_m) * s;
+    const long long waves = (units + sms - 1) / sms;
+    const double fill = static_cast<double>(units) / static_cast<double>(waves * sms);
+    const double per = static_cast<double>(num_n) / s;
+    const double balance = per / static_cast<double>((num_n + s - 1) / s);
+    const double eff = fill * balance;
+    if (eff > best_eff + 1e-3) {
+      best_eff = eff;
+      best = s;
+    }
+  }
+  return best;
+}
+
+// --------------------------------------------------------- aux kernels ---
+
+__device__ __forceinline__ Part part_identity() {
+  Part p;
+  p.m = NEG_BIG;
+  p.s = 0.f;
+  p.w = 0.f;
+  p.best = -INFINITY;
+  p.idx = 0x7fffffff;
+  p.zy = -INFINITY;
+  return p;
+}
+
+__device__ __forceinline__ void part_merge(Part& a, const Part& b) {
+  const float mx = fmaxf(a.m, b.m);
+  const float da = a.m - mx, db = b.m - mx;
+  const float ea = ex2_approx(da * LOG2E), eb = ex2_approx(db * LOG2E);
+  const float s = a.s * ea + b.s * eb;
+  const float w = ea * fmaf(da, a.s, a.w) + eb * fmaf(db, b.s, b.w);
+  a.m = mx;
+  a.s = s;
+  a.w = w;
+  if (b.best > a.best || (b.best == a.best && b.idx < a.idx)) {
+    a.best = b.best;
+    a.idx = b.idx;
+  }
+  a.zy = fmaxf(a.zy, b.zy);
+}
+
+__device__ __forceinline__ Part part_shfl_down(const Part& a, int off) {
+  Part b;
+  b.m = __shfl_down_sync(0xffffffffu, a.m, off);
+  b.s = __shfl_down_sync(0xffffffffu, a.s, off);
+  b.w = __shfl_down_sync(0xffffffffu, a.w, off);
+  b.best = __shfl_down_sync(0xffffffffu, a.best, off);
+  b.idx = __shfl_down_sync(0xffffffffu, a.idx, off);
+  b.zy = __shfl_down_sync(0xffffffffu, a.zy, off);
+  return b;
+}
+
+// One warp per token: lanes merge strided subsets of the records, then a
+// fixed-shape shuffle tree (deterministic). FINAL=false writes the merged
+// record; FINAL=true writes lse / nll / entropy / argmax.
+template <bool FINAL>
+__global__ void __launch_bounds__(256) stats_merge_kernel(const Part* __restrict__ parts, int n_parts,
+                                                          long long tok_stride, long long part_stride,
+                                                          int n_tokens, Part* __restrict__ rec_out,
+                                                          const int64_t* __restrict__ labels,
+                                                          float* __restrict__ lse_out, float* __restrict__ nll_out,
+                                                          float* __restrict__ ent_out,
+                                                          int64_t* __restrict__ arg_out, int* err) {
+  const int lane = threadIdx.x & 31;
+  const int warps_per_block = blockDim.x / 32;
+  for (int t = blockIdx.x * warps_per_block + threadIdx.x / 32; t < n_tokens; t += gridDim.x * warps_per_block) {
+    Part acc = part_identity();
+    for (int pi = lane; pi < n_parts; pi += 32) {
+      const Part* src = parts + static_cast<long long>(t) * tok_stride + static_cast<long long>(pi) * part_stride;
+      const float2 a = reinterpret_cast<const float2*>(src)[0];
+      const float2 b = reinterpret_cast<const float2*>(src)[1];
+      const float2 c = reinterpret_cast<const float2*>(src)[2];
+      Part q;
+      q.m = a.x;
+      q.s = a.y;
+      q.w = b.x;
+      q.best = b.y;
+      q.idx = __float_as_int(c.x);
+      q.zy = c.y;
+      part_merge(acc, q);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const Part o = part_shfl_down(acc, off);
+      part_merge(acc, o);
+    }
+    if (lane == 0) {
+      if constexpr (!FINAL) {
+        float2* d = reinterpret_cast<float2*>(rec_out + t);
+        d[0] = make_float2(acc.m, acc.s);
+        d[1] = make_float2(acc.w, acc.best);
+        d[2] = make_float2(__int_as_float(acc.idx), acc.zy);
+      } else {
+        const float ln_s = lg2_approx(acc.s) * LN2;
+        const float lse = acc.m + ln_s;
+        const float ent = ln_s - acc.w / acc.s;
+        const int64_t y = labels[t];
+        float nll = 0.f;
+        if (y != -100) {
+          if (acc.zy == -INFINITY) {
+            nll = __int_as_float(0x7fc00000);  // NaN: target outside [0, V)
+            raise_error(err, ERR_LABEL);
+          } else {
+            nll = lse - acc.zy;
+          }
+        }
+        lse_out[t] = lse;
+        nll_out[t] = nll;
+        ent_out[t] = ent;
+        arg_out[t] = static_cast<int64_t>(acc.idx);
+      }
+    }
+  }
+}
+
+// Deterministic loss: one block, fixed per-thread strided partial sums, fixed tree.
+__global__ void __launch_bounds__(1024) loss_kernel(const float* __restrict__ nll, const int64_t* __restrict__ labels,
+                                                    int n_tokens, const float* num_items_dev, float num_items,
+                                                    float* loss, float* denom_out) {
+  __shared__ float s_sum[32];
+  __shared__ int s_cnt[32];
+  float sum = 0.f;
+  int cnt = 0;
+  for (int t = threadIdx.x; t < n_tokens; t += blockDim.x) {
+    sum += nll[t];
+    cnt += labels[t] != -100 ? 1 : 0;
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    sum += __shfl_down_sync(0xffffffffu, sum, off);
+    cnt += __shfl_down_sync(0xffffffffu, cnt, off);
+  }
+  const int w = threadIdx.x / 32;
+  if ((threadIdx.x & 31) == 0) {
+    s_sum[w] = sum;
+    s_cnt[w] = cnt;
+  }
+  __syncthreads();
+  if (w == 0) {
+    const int nw = blockDim.x / 32;
+    sum = threadIdx.x < nw ? s_sum[threadIdx.x] : 0.f;
+    cnt = threadIdx.x < nw ? s_cnt[threadIdx.x] : 0;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      sum += __shfl_down_sync(0xffffffffu, sum, off);
+      cnt += __shfl_down_sync(0xffffffffu, cnt, off);
+    }
+    if (threadIdx.x == 0) {
+      float d = num_items_dev ? *num_items_dev : (num_items >= 0.f ? num_items : static_cast<float>(cnt));
+      d = fmaxf(d, 1.0f);
+      *denom_out = d;
+      *loss = sum / d;
+    }
+  }
+}
+
+// Stable compaction of tokens with label != -100 (one block).
+__global__ void __launch_bounds__(1024) compact_kernel(const int64_t* __restrict__ labels, int n_tokens,
+                                                       long long v_off, int v_local, const float* __restrict__ lse,
+                                                       int* __restrict__ count, int* __restrict__ row_idx,
+                                                       int* __restrict__ lbl_lab, float* __restrict__ lse_lab) {
+  __shared__ int s_warp[32];
+  const int per = (n_tokens + blockDim.x - 1) / blockDim.x;
+  const int t0 = threadIdx.x * per;
+  const int t1 = min(t0 + per, n_tokens);
+  int c = 0;
+  for (int t = t0; t < t1; ++t) c += labels[t] != -100 ? 1 : 0;
+  // block exclusive scan of c
+  const int lane = threadIdx.x & 31, w = threadIdx.x / 32;
+  int incl = c;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int o = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += o;
+  }
+  if (lane == 31) s_warp[w] = incl;
+  __syncthreads();
+  if (w == 0) {
+    const int nw = blockDim.x / 32;
+    int v = lane < nw ? s_warp[lane] : 0;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, v, off);
+      if (lane >= off) v += o;
+    }
+    if (lane < nw) s_warp[lane] = v;  // inclusive warp totals
+  }
+  __syncthreads();
+  int pos = incl - c + (w > 0 ? s_warp[w - 1] : 0);
+  for (int t = t0; t < t1; ++t) {
+    const int64_t y = labels[t];
+    if (y != -100) {
+      const long long yl = y - v_off;
+      row_idx[pos] = t;
+      lbl_lab[pos] = (yl >= 0 && yl < v_local) ? static_cast<int>(yl) : -1;
+      lse_lab[pos] = lse[t];
+      ++pos;
+    }
+  }
+  if (threadIdx.x == blockDim.x - 1) *count = pos;
+}
+
+// X_lab[r] = X[row_idx[r]] for r < count, zero rows for count <= r < rows_pad. 16-byte vectors.
+__global__ void gather_rows_kernel(const uint4* __restrict__ x, int vec_per_row, const int* __restrict__ count,
+                                   const int* __restrict__ row_idx, int rows_pad, uint4* __restrict__ out) {
+  const int n = *count;
+  const long long total = static_cast<long long>(rows_pad) * vec_per_row;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int r = static_cast<int>(i / vec_per_row);
+    const int c = static_cast<int>(i % vec_per_row);
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r < n) v = x[static_cast<long long>(row_idx[r]) * vec_per_row + c];
+    out[i] = v;
+  }
+}
+
+template <bool BF16>
+__global__ void dx_finalize_kernel(const float4* __restrict__ src, long long n4, uint2* __restrict__ dst) {
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const float4 v = src[i];
+    uint2 o;
+    o.x = pack2<BF16>(v.x, v.y);
+    o.y = pack2<BF16>(v.z, v.w);
+    dst[i] = o;
+  }
+}
+
+__global__ void selftest_wait_kernel(unsigned long long timeout_ns, int* err) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    // Nothing ever arrives on `bar`: the bounded wait must give up.
+    if (!mbar_wait(&bar, 0, &abort_flag, timeout_ns)) raise_error(err, ERR_TIMEOUT);
+    // Complete the phase so the barrier is left in a clean state.
+    mbar_arrive(&bar);
+  }
+  __syncthreads();
+}
+
+// ------------------------------------------------------------ workspace ---
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+struct BwdLayout {
+  size_t count, row_idx, lbl_lab, lse_lab, x_lab, g, dx_acc, total;
+  int rows_pad, v_chunk;
+};
+
+BwdLayout bwd_layout(int64_t n, int64_t h, int64_t v_local, int64_t v_chunk) {
+  BwdLayout L{};
+  int64_t vc = v_chunk <= 0 ? 8192 : v_chunk;
+  vc = (vc + 255) / 256 * 256;
+  const int64_t vmax = (v_local + 255) / 256 * 256;
+  if (vc > vmax) vc = vmax;
+  if (vc < 256) vc = 256;
+  L.v_chunk = static_cast<int>(vc);
+  L.rows_pad = static_cast<int>((n + BM - 1) / BM * BM);
+  size_t off = 0;
+  L.count = off;
+  off = align_up(off + 16, 256);
+  L.row_idx = off;
+  off = align_up(off + sizeof(int) * n, 256);
+  L.lbl_lab = off;
+  off = align_up(off + sizeof(int) * n, 256);
+  L.lse_lab = off;
+  off = align_up(off + sizeof(float) * n, 256);
+  L.x_lab = off;
+  off = align_up(off + 2ull * L.rows_pad * h, 256);
+  L.g = off;
+  off = align_up(off + 2ull * L.rows_pad * vc, 256);
+  L.dx_acc = off;
+  off = align_up(off + 4ull * L.rows_pad * h, 256);
+  L.total = off;
+  return L;
+}
+
+bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
+
+}  // namespace
+
+// =================================================================== C ABI ===
+
+extern "C" {
+
+int lmce_abi_version(void) { return LMCE_ABI_VERSION; }
+
+const char* lmce_last_error(void) { return t_err; }
+
+int lmce_device_error(int reset) {
+  DevInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+  int v = 0;
+  LMCE_CUDA(cudaMemcpy(&v, d->err_ptr, sizeof(int), cudaMemcpyDeviceToHost));
+  if (reset) {
+    const int z = 0;
+    LMCE_CUDA(cudaMemcpy(d->err_ptr, &z, sizeof(int), cudaMemcpyHostToDevice));
+  }
+  if (v != 0) fail(v, "device error word = %d", v);
+  return v;
+}
+
+int64_t lmce_fwd_num_parts(int64_t n_tokens, int64_t vocab_local) {
+  DevInfo* d = nullptr;
+  int sms = 148;
+  if (device_info(&d) == LMCE_OK) sms = d->sms;
+  if (n_tokens <= 0 || vocab_local <= 0) return 1;
+  const int num_m = static_cast<int>((n_tokens + BM - 1) / BM);
+  const int num_n = static_cast<int>((vocab_local + kBN - 1) / kBN);
+  return choose_slabs(num_m, num_n, sms);
+}
+
+int lmce_fwd_stats(const void* hidden, const void* weight, const int64_t* labels, int64_t n_tokens,
+                   int64_t hidden_dim, int64_t vocab_local, int64_t vocab_offset, int dtype, lmce_part* parts,
+                   int64_t n_parts, void* stream) {
+  if (!hidden || !weight || !labels || !parts) return fail(LMCE_ERR_INVALID_ARGUMENT, "null pointer");
+  if (n_tokens <= 0 || n_tokens > (1ll << 30)) return fail(LMCE_ERR_INVALID_ARGUMENT, "bad n_tokens %lld", (long long)n_tokens);
+  if (vocab_local <= 0 || vocab_local + vocab_offset > (1ll << 31) - 1 || vocab_offset < 0)
+    return fail(LMCE_ERR_INVALID_ARGUMENT, "bad vocab size/offset");
+  if (hidden_dim <= 0 || hidden_dim % 64 != 0) return fail(LMCE_ERR_UNSUPPORTED, "hidden_dim must be a positive multiple of 64");
+  if (dtype != LMCE_DTYPE_F16 && dtype != LMCE_DTYPE_BF16) return fail(LMCE_ERR_UNSUPPORTED, "dtype %d", dtype);
+  DevInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+  if (int rc = get_encoder()) return rc;
+  const int num_m = static_cast<int>((n_tokens + BM - 1) / BM);
+  const int num_n = static_cast<int>((vocab_local + kBN - 1) / kBN);
+  if (n_parts < 1 || n_parts > num_n) return fail(LMCE_ERR_INVALID_ARGUMENT, "n_parts %lld out of range", (long long)n_parts);
+  const bool bf16 = dtype == LMCE_DTYPE_BF16;
+  CUtensorMap ma, mb;
+  if (int rc = make_map(&ma, hidden, bf16, hidden_dim, n_tokens, hidden_dim, BM)) return rc;
+  if (int rc = make_map(&mb, weight, bf16, hidden_dim, vocab_local, hidden_dim, kBN)) return rc;
+  EngineParams p{};
+  p.M = static_cast<int>(n_tokens);
+  p.N = static_cast<int>(vocab_local);
+  p.K = static_cast<int>(hidden_dim);
+  p.n_slabs = static_cast<int>(n_parts);
+  p.v_limit = static_cast<int>(vocab_local);
+  p.labels = labels;
+  p.label_off = vocab_offset;
+  p.parts = reinterpret_cast<Part*>(parts);
+  p.err = d->err_ptr;
+  p.timeout_ns = wait_timeout_ns();
+  const long long units = static_cast<long long>(num_m) * n_parts;
+  const int grid = static_cast<int>(units < d->sms ? units : d->sms);
+  return launch_engine_dt<KIND_STATS, false, false>(bf16, ma, mb, p, grid, static_cast<cudaStream_t>(stream));
+}
+
+int lmce_stats_reduce(const lmce_part* parts, int64_t n_parts, int64_t tok_stride, int64_t part_stride,
+                      int64_t n_tokens, lmce_part* record_out, void* stream) {
+  if (!parts || !record_out || n_parts < 1 || n_tokens < 1) return fail(LMCE_ERR_INVALID_ARGUMENT, "bad arguments");
+  DevInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+  const int warps = 8;
+  long long blocks = (n_tokens + warps - 1) / warps;
+  if (blocks > 65535ll * 4) blocks = 65535ll * 4;
+  stats_merge_kernel<false><<<static_cast<int>(blocks), warps * 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const Part*>(parts), static_cast<int>(n_parts), tok_stride, part_stride,
+      static_cast<int>(n_tokens), reinterpret_cast<Part*>(record_out), nullptr, nullptr, nullptr, nullptr, nullptr,
+      d->err_ptr);
+  LMCE_CUDA(cudaGetLastError());
+  return LMCE_OK;
+}
+
+int lmce_stats_finish(const lmce_part* parts, int64_t n_parts, int64_t tok_stride, int64_t part_stride,
+                      const int64_t* labels, int64_t n_tokens, const float* num_items_dev, double num_items,
+                      float* lse, float* nll, float* entropy, int64_t* argmax, float* loss, float* denom,
+                      void* stream) {
+  if (!parts || !labels || !lse || !nll || !entropy || !argmax || !loss || !denom || n_parts < 1 || n_tokens < 1)
+    return fail(LMCE_ERR_INVALID_ARGUMENT, "bad arguments");
+  DevInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int warps = 8;
+  long long blocks = (n_tokens + warps - 1) / warps;
+  if (blocks > 65535ll * 4) blocks = 65535ll * 4;
+  stats_merge_kernel<true><<<static_cast<int>(blocks), warps * 32, 0, st>>>(
+      reinterpret_cast<const Part*>(parts), static_cast<int>(n_parts), tok_stride, part_stride,
+      static_cast<int>(n_tokens), nullptr, labels, lse, nll, entropy, argmax, d->err_ptr);
+  LMCE_CUDA(cudaGetLastError());
+  loss_kernel<<<1, 1024, 0, st>>>(nll, labels, static_cast<int>(n_tokens), num_items_dev,
+                                  static_cast<float>(num_items), loss, denom);
+  LMCE_CUDA(cudaGetLastError());
+  return LMCE_OK;
+}
+
+size_t lmce_bwd_workspace_bytes(int64_t n_tokens, int64_t hidden_dim, int64_t vocab_local, int64_t v_chunk) {
+  if (n_tokens <= 0 || hidden_dim <= 0 || vocab_local <= 0) return 0;
+  return bwd_layout(n_tokens, hidden_dim, vocab_local, v_chunk).total;
+}
+
+int lmce_backward(const void* hidden, const void* weight, const int64_t* labels, const float* lse,
+                  int64_t n_tokens, int64_t hidden_dim, int64_t vocab_local, int64_t vocab_offset, int dtype,
+                  const float* grad_loss, const float* denom, void* d_hidden, float* d_hidden_f32,
+                  void* d_weight, int64_t v_chunk, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!hidden || !weight || !labels || !lse || !denom || !workspace)
+    return fail(LMCE_ERR_INVALID_ARGUMENT, "null pointer");
+  if (n_tokens <= 0 || n_tokens > (1ll << 30)) return fail(LMCE_ERR_INVALID_ARGUMENT, "bad n_tokens");
+  if (vocab_local <= 0 || vocab_offset < 0 || vocab_local + vocab_offset > (1ll << 31) - 1)
+    return fail(LMCE_ERR_INVALID_ARGUMENT, "bad vocab size/offset");
+  if (hidden_dim <= 0 || hidden_dim % 64 != 0) return fail(LMCE_ERR_UNSUPPORTED, "hidden_dim must be a positive multiple of 64");
+  if (dtype != LMCE_DTYPE_F16 && dtype != LMCE_DTYPE_BF16) return fail(LMCE_ERR_UNSUPPORTED, "dtype %d", dtype);
+  if ((d_hidden && !aligned16(d_hidden)) || (d_hidden_f32 && !aligned16(d_hidden_f32)) ||
+      (d_weight && !aligned16(d_weight)) || !aligned16(workspace))
+    return fail(LMCE_ERR_INVALID_ARGUMENT, "output/workspace buffers must be 16-byte aligned");
+  const BwdLayout L = bwd_layout(n_tokens, hidden_dim, vocab_local, v_chunk);
+  if (workspace_bytes < L.total)
+    return fail(LMCE_ERR_WORKSPACE, "workspace %zu bytes < required %zu", workspace_bytes, L.total);
+  DevInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+  if (int rc = get_encoder()) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool bf16 = dtype == LMCE_DTYPE_BF16;
+  const int n = static_cast<int>(n_tokens), h = static_cast<int>(hidden_dim), vl = static_cast<int>(vocab_local);
+  char* ws = static_cast<char*>(workspace);
+  int* count = reinterpret_cast<int*>(ws + L.count);
+  int* row_idx = reinterpret_cast<int*>(ws + L.row_idx);
+  int* lbl_lab = reinterpret_cast<int*>(ws + L.lbl_lab);
+  float* lse_lab = reinterpret_cast<float*>(ws + L.lse_lab);
+  void* x_lab = ws + L.x_lab;
+  void* g = ws + L.g;
+  float* dx_acc = reinterpret_cast<float*>(ws + L.dx_acc);
+
+  if (d_hidden) LMCE_CUDA(cudaMemsetAsync(d_hidden, 0, 2ull * n * h, st));
+
+  compact_kernel<<<1, 1024, 0, st>>>(labels, n, vocab_offset, vl, lse, count, row_idx, lbl_lab, lse_lab);
+  LMCE_CUDA(cudaGetLastError());
+  {
+    const int vec = h * 2 / 16;
+    const long long total = static_cast<long long>(L.rows_pad) * vec;
+    long long blocks = (total + 255) / 256;
+    if (blocks > d->sms * 8ll) blocks = d->sms * 8ll;
+    gather_rows_kernel<<<static_cast<int>(blocks), 256, 0, st>>>(static_cast<const uint4*>(hidden), vec, count,
+                                                                 row_idx, L.rows_pad, static_cast<uint4*>(x_lab));
+    LMCE_CUDA(cudaGetLastError());
+  }
+
+  const bool want_dx = d_hidden != nullptr || d_hidden_f32 != nullptr;
+  const bool want_dw = d_weight != nullptr;
+  if (!want_dx && !want_dw) return LMCE_OK;
+
+  // Tensor maps (chunk offsets are applied as TMA coordinates).
+  CUtensorMap m_xlab_k, m_w_k, m_g_k, m_w_mn, m_g_mn, m_xlab_mn;
+  if (int rc = make_map(&m_xlab_k, x_lab, bf16, h, L.rows_pad, h, BM)) return rc;
+  if (int rc = make_map(&m_w_k, weight, bf16, h, vl, h, kBN)) return rc;
+  if (int rc = make_map(&m_g_k, g, bf16, L.v_chunk, L.rows_pad, L.v_chunk, BM)) return rc;
+  if (int rc = make_map(&m_w_mn, weight, bf16, h, vl, h, 64)) return rc;
+  if (int rc = make_map(&m_g_mn, g, bf16, L.v_chunk, L.rows_pad, L.v_chunk, 64)) return rc;
+  if (int rc = make_map(&m_xlab_mn, x_lab, bf16, h, L.rows_pad, h, 64)) return rc;
+
+  EngineParams base{};
+  base.err = d->err_ptr;
+  base.timeout_ns = wait_timeout_ns();
+  base.grad_loss = grad_loss;
+  base.denom = denom;
+  base.gscale = 32768.0f;
+
+  const int n_chunks = (vl + L.v_chunk - 1) / L.v_chunk;
+  const int grid = d->sms;
+  for (int c = 0; c < n_chunks; ++c) {
+    const int start = c * L.v_chunk;
+    const int width = (vl - start) < L.v_chunk ? (vl - start) : L.v_chunk;
+
+    EngineParams pg = base;  // G = (softmax - onehot) * 2^15
+    pg.M = L.rows_pad;
+    pg.count_dev = count;
+    pg.N = width;
+    pg.K = h;
+    pg.b_off = start;
+    pg.v_limit = width;
+    pg.lbl_lab = lbl_lab;
+    pg.lse_lab = lse_lab;
+    pg.out = g;
+    pg.ldo = L.v_chunk;
+    if (int rc = launch_engine_dt<KIND_GRAD, false, false>(bf16, m_xlab_k, m_w_k, pg, grid, st)) return rc;
+
+    if (want_dx) {
+      EngineParams px = base;  // dX += G . W_chunk
+      px.M = L.rows_pad;
+      px.count_dev = count;
+      px.N = h;
+      px.K = width;
+      px.b_off = start;
+      px.out = d_hidden;
+      px.out_f32 = d_hidden_f32;
+      px.acc_f32 = dx_acc;
+      px.row_idx = row_idx;
+      px.ldo = h;
+      px.first = c == 0;
+      px.last = c == n_chunks - 1;
+      if (int rc = launch_engine_dt<KIND_DX, false, true>(bf16, m_g_k, m_w_mn, px, grid, st)) return rc;
+    }
+    if (want_dw) {
+      EngineParams pw = base;  // dW_chunk = G^T . X_lab
+      pw.M = width;
+      pw.count_dev = count;
+      pw.N = h;
+      pw.K = L.rows_pad;
+      pw.b_off = start;
+      pw.v_limit = width;
+      pw.out = d_weight;
+      pw.ldo = h;
+      if (int rc = launch_engine_dt<KIND_DW, true, true>(bf16, m_g_mn, m_xlab_mn, pw, grid, st)) return rc;
+    }
+  }
+  return LMCE_OK;
+}
+
+int lmce_dx_finalize(const float* d_hidden_f32, int64_t n_tokens, int64_t hidden_dim, int dtype, void* d_hidden,
+                     void* stream) {
+  if (!d_hidden_f32 || !d_hidden || n_tokens <= 0 || hidden_dim <= 0 || hidden_dim % 4 != 0)
+    return fail(LMCE_ERR_INVALID_ARGUMENT, "bad arguments");
+  if (!aligned16(d_hidden_f32) || reinterpret_cast<uintptr_t>(d_hidden) % 8 != 0)
+    return fail(LMCE_ERR_INVALID_ARGUMENT, "misaligned buffers");
+  DevInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+  const long long n4 = n_tokens * hidden_dim / 4;
+  long long blocks = (n4 + 255) / 256;
+  if (blocks > d->sms * 8ll) blocks = d->sms * 8ll;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == LMCE_DTYPE_BF16)
+    dx_finalize_kernel<true><<<static_cast<int>(blocks), 256, 0, st>>>(reinterpret_cast<const float4*>(d_hidden_f32),
+                                                                       n4, static_cast<uint2*>(d_hidden));
+  else if (dtype == LMCE_DTYPE_F16)
+    dx_finalize_kernel<false><<<static_cast<int>(blocks), 256, 0, st>>>(
+        reinterpret_cast<const float4*>(d_hidden_f32), n4, static_cast<uint2*>(d_hidden));
+  else
+    return fail(LMCE_ERR_UNSUPPORTED, "dtype %d", dtype);
+  LMCE_CUDA(cudaGetLastError());
+  return LMCE_OK;
+}
+
+int lmce_selftest_wait_timeout(uint64_t timeout_ns, void* stream) {
+  DevInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+  selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(timeout_ns, d->err_ptr);
+  LMCE_CUDA(cudaGetLastError());
+  return LMCE_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,187 @@
+"""Parity of the sm_100a head (rus_b200.chunked_lm_head -> liblmce.so) against the oracle.
+
+Tolerances:
+  loss, lse, nll      1e-3 relative per token (absolute floor 1e-3 for values near 0)
+  entropy             |d| <= 1e-3 * max(|ref|, 1)
+  dX, dW              1e-2 relative L2
+  argmax              bit-exact except where the two candidates' logits lie within
+                      max(1e-3, one ulp of the input dtype) (oracle.argmax_mismatch_ok)
+The reference's own known-answer test (solution/test_kernels.py:189-226) is also
+run with its own tolerances (loss 2e-3, dX 5e-3, entropy 2e-3, argmax exact).
+"""
+from __future__ import annotations
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from oracle import lmce_oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+
+def _run_ours(hidden, labels, weight, num_items=None, v_chunk=8192, want_dw=True):
+    from rus_b200 import chunked_lm_head
+
+    h = hidden.detach().clone().requires_grad_(True)
+    w = weight.detach().clone().requires_grad_(want_dw)
+    loss, nll, ent, arg = chunked_lm_head(h, labels, w, num_items, v_chunk)
+    loss.backward()
+    torch.cuda.synchronize()
+    from rus_b200 import _lib
+
+    assert _lib.device_error(reset=True) == 0
+    return dict(loss=loss.detach(), nll=nll, entropy=ent, argmax=arg, dX=h.grad, dW=w.grad if want_dw else None)
+
+
+def _close_per_token(ours, ref, rtol=1e-3, floor=1e-3):
+    ours = ours.double().cpu()
+    ref = ref.double().cpu()
+    bad = (ours - ref).abs() > rtol * torch.maximum(ref.abs(), torch.full_like(ref, floor / rtol))
+    return int(bad.sum())
+
+
+def _check_contract(ours, ref, logits32, dtype, check_dw=True):
+    assert torch.isfinite(ours["loss"]).item()
+    assert _close_per_token(ours["loss"].reshape(1), ref["loss"].reshape(1)) == 0, (ours["loss"], ref["loss"])
+    assert _close_per_token(ours["nll"], ref["nll"]) == 0
+    ent_o, ent_r = ours["entropy"].double().cpu(), ref["entropy"].double().cpu()
+    assert ((ent_o - ent_r).abs() <= 1e-3 * torch.clamp(ent_r.abs(), min=1.0)).all()
+    ok = orc.argmax_mismatch_ok(ours["argmax"], ref["argmax"], logits32, dtype)
+    assert bool(ok.all()), f"{int((~ok).sum())} argmax mismatches beyond the tie rule"
+    assert orc.rel_l2(ours["dX"].float(), ref["dX"].float()) < 1e-2
+    if check_dw:
+        assert orc.rel_l2(ours["dW"].float(), ref["dW"].float()) < 1e-2
+
+
+def test_reference_known_answer(cuda_device):
+    """solution/test_kernels.py:189-226 with its own inputs and tolerances."""
+    torch.manual_seed(3)
+    B, S, D, V = 2, 32, 256, 4099
+    hidden = torch.randn((B, S, D), dtype=torch.float16)
+    weight = torch.randn((V, D), dtype=torch.float16) * 0.02
+    labels = torch.randint(0, V, (B, S), dtype=torch.long)
+    labels[:, :8] = -100
+    shift = torch.full((B, S), -100, dtype=torch.long)
+    shift[:, :-1] = labels[:, 1:]
+
+    ref = orc.eager_head(hidden, shift, weight)  # CPU oracle
+    ours = _run_ours(hidden.to(cuda_device), shift.to(cuda_device), weight.to(cuda_device), v_chunk=1024)
+
+    torch.testing.assert_close(ours["loss"].cpu(), ref["loss"], rtol=2e-3, atol=2e-3)
+    torch.testing.assert_close(ours["dX"].float().cpu().view(B * S, D), ref["dX"].float(), rtol=5e-3, atol=5e-3)
+    torch.testing.assert_close(ours["entropy"].cpu(), ref["entropy"], rtol=2e-3, atol=2e-3)
+    assert torch.equal(ours["argmax"].cpu(), ref["argmax"])
+    torch.testing.assert_close(ours["dW"].float().cpu(), ref["dW"].float(), rtol=5e-3, atol=5e-3)
+
+
+EDGE_CASES = [
+    # (N, H, V, dtype, label pattern)
+    (1, 64, 300, torch.float16, "all_valid"),
+    (130, 128, 1000, torch.bfloat16, "half_masked"),
+    (257, 192, 5000, torch.float16, "half_masked"),
+    (64, 64, 100, torch.float16, "all_valid"),  # V smaller than one vocab tile
+    (200, 256, 4099, torch.float16, "all_masked"),
+    (384, 320, 2560, torch.bfloat16, "random"),
+]
+
+
+@pytest.mark.parametrize("n,h,v,dtype,pattern", EDGE_CASES)
+def test_edge_cases(cuda_device, n, h, v, dtype, pattern):
+    g = torch.Generator().manual_seed(n * 7 + h + v)
+    hidden = torch.randn(n, h, generator=g).to(dtype)
+    weight = (torch.randn(v, h, generator=g) * (2.0 / h ** 0.5)).to(dtype)
+    labels = torch.randint(0, v, (n,), generator=g)
+    if pattern == "half_masked":
+        labels[: n // 2] = -100
+    elif pattern == "all_masked":
+        labels[:] = -100
+    elif pattern == "random":
+        labels[torch.rand(n, generator=g) < 0.3] = -100
+    ref = orc.eager_head(hidden, labels, weight, grad_mode="fp32")
+    ours = _run_ours(hidden.to(cuda_device), labels.to(cuda_device), weight.to(cuda_device), v_chunk=512)
+    logits32 = hidden.float() @ weight.float().t()
+    if pattern == "all_masked":
+        assert ours["loss"].item() == 0.0
+        assert float(ours["nll"].abs().max()) == 0.0
+        assert float(ours["dX"].float().abs().max()) == 0.0
+        assert float(ours["dW"].float().abs().max()) == 0.0
+        ent_o, ent_r = ours["entropy"].double().cpu(), ref["entropy"].double()
+        assert ((ent_o - ent_r).abs() <= 1e-3 * torch.clamp(ent_r.abs(), min=1.0)).all()
+        return
+    _check_contract(ours, ref, logits32, dtype)
+
+
+@pytest.mark.parametrize("kind", ["int", "tensor"])
+def test_num_items_in_batch(cuda_device, kind):
+    g = torch.Generator().manual_seed(11)
+    n, h, v = 96, 128, 3000
+    hidden = torch.randn(n, h, generator=g).half()
+    weight = (torch.randn(v, h, generator=g) * 0.05).half()
+    labels = torch.randint(0, v, (n,), generator=g)
+    labels[::3] = -100
+    num_items = 500 if kind == "int" else torch.tensor(500, device=cuda_device)
+    ref = orc.eager_head(hidden, labels, weight, num_items_in_batch=500, grad_mode="fp32")
+    ours = _run_ours(hidden.to(cuda_device), labels.to(cuda_device), weight.to(cuda_device), num_items=num_items)
+    _check_contract(ours, ref, hidden.float() @ weight.float().t(), torch.float16)
+
+
+@pytest.mark.parametrize("v_chunk", [256, 1024, 8192])
+def test_v_chunk_invariance(cuda_device, v_chunk):
+    """The backward's vocab chunking must not change the result beyond rounding."""
+    g = torch.Generator().manual_seed(5)
+    n, h, v = 300, 256, 9000
+    hidden = torch.randn(n, h, generator=g).half().to(cuda_device)
+    weight = (torch.randn(v, h, generator=g) * 0.05).half().to(cuda_device)
+    labels = torch.randint(0, v, (n,), generator=g).to(cuda_device)
+    a = _run_ours(hidden, labels, weight, v_chunk=v_chunk)
+    b = _run_ours(hidden, labels, weight, v_chunk=v)
+    assert orc.rel_l2(a["dX"].float(), b["dX"].float()) < 2e-3
+    assert orc.rel_l2(a["dW"].float(), b["dW"].float()) < 2e-3
+    assert torch.equal(a["argmax"], b["argmax"])
+
+
+@pytest.mark.parametrize("cfg,n_override", [("c1", None), ("c5", 600), ("c4", 256), ("c3", 256)])
+def test_config_parity(cuda_device, cfg, n_override):
+    """BASELINE.json configs (full H and V), against the reference eager path run on the GPU."""
+    X, y, W, meta = orc.make_config_inputs(cfg, seed=0, device="cpu", n_override=n_override)
+    Xd, yd, Wd = X.to(cuda_device), y.to(cuda_device), W.to(cuda_device)
+    ref = orc.eager_head(Xd, yd, Wd, grad_mode="fp32")
+    ours = _run_ours(Xd, yd, Wd)
+    logits32 = (Xd.float() @ Wd.float().t())
+    _check_contract(ours, ref, logits32, X.dtype)
+    del logits32
+
+
+def test_c1_against_cpu_oracle(cuda_device):
+    """Config 1 at full size against the CPU oracle (eager formula, fp32 gradients)."""
+    X, y, W, meta = orc.make_config_inputs("c1", seed=0)
+    ref = orc.eager_head(X, y, W, grad_mode="fp32")
+    ours = _run_ours(X.to(cuda_device), y.to(cuda_device), W.to(cuda_device))
+    _check_contract(ours, ref, X.float() @ W.float().t(), X.dtype)
+
+
+def test_forward_only_and_no_grad(cuda_device):
+    from rus_b200 import chunked_lm_head
+
+    g = torch.Generator().manual_seed(9)
+    hidden = torch.randn(50, 128, generator=g).half().to(cuda_device)
+    weight = (torch.randn(700, 128, generator=g) * 0.05).half().to(cuda_device)
+    labels = torch.randint(0, 700, (50,), generator=g).to(cuda_device)
+    with torch.no_grad():
+        loss, nll, ent, arg = chunked_lm_head(hidden, labels, weight)
+    ref = orc.eager_head(hidden.cpu(), labels.cpu(), weight.cpu(), grads=False)
+    assert abs(loss.item() - ref["loss"].item()) <= 1e-3 * abs(ref["loss"].item())
+    assert nll.shape == (50,) and ent.dtype == torch.float32 and arg.dtype == torch.int64
+    assert not nll.requires_grad and not arg.requires_grad
+
+
+def test_timeout_path_reports_error(cuda_device):
+    """A bounded wait that nothing satisfies returns LMCE_ERR_TIMEOUT instead of hanging."""
+    from rus_b200 import _lib
+
+    _lib.device_error(reset=True)
+    _lib.call("lmce_selftest_wait_timeout", 50_000_000, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert _lib.device_error(reset=True) == _lib.LMCE_ERR_TIMEOUT
+    assert _lib.device_error(reset=True) == 0
