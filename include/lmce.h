@@ -132,6 +132,9 @@ LMCE_API int lmce_dx_finalize(const float* d_hidden_f32, int64_t n_tokens, int64
 
 /* ------------------------------------------------------------ diagnostics */
 
+/* Number of kernels this library has launched in this process (all devices). */
+LMCE_API uint64_t lmce_launch_count(void);
+
 /* Launches a kernel whose bounded wait is never satisfied; after timeout_ns it
  * records LMCE_ERR_TIMEOUT in the device error word and returns normally.
  * Exercises the failure path without hanging or faulting the GPU. */

@@ -64,6 +64,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "lmce_dx_finalize": (_int, [_vp, _i64, _i64, _int, _vp, _vp]),
     "lmce_selftest_wait_timeout": (_int, [ctypes.c_uint64, _vp]),
+    "lmce_launch_count": (ctypes.c_uint64, []),
 }
 
 _lock = threading.Lock()
@@ -102,6 +103,11 @@ def call(name: str, *args) -> int:
     rc = fn(*args)
     check(rc)
     return rc
+
+
+def launch_count() -> int:
+    """Kernels launched by liblmce.so in this process so far."""
+    return int(load().lmce_launch_count())
 
 
 def device_error(reset: bool = True) -> int:

@@ -10,6 +10,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 
 #include "../../include/lmce.h"
@@ -25,6 +26,18 @@ __device__ int g_lmce_err;
 namespace {
 
 thread_local char t_err[512] = "";
+std::atomic<unsigned long long> g_launches{0};
+
+// Every kernel launch in this file goes through this check, which also counts it.
+int launched() {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    std::snprintf(t_err, sizeof(t_err), "kernel launch failed: %s", cudaGetErrorString(e));
+    return LMCE_ERR_CUDA;
+  }
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return LMCE_OK;
+}
 
 int fail(int code, const char* fmt, ...) {
   va_list ap;
@@ -91,16 +104,12 @@ PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
 int get_encoder() {
   static std::once_flag once;
-  static int status = LMCE_OK;
   std::call_once(once, [] {
     cudaDriverEntryPointQueryResult q;
     void* fn = nullptr;
     cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
-    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr) {
-      status = fail(LMCE_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
-      return;
-    }
-    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    if (e == cudaSuccess && q == cudaDriverEntryPointSuccess && fn != nullptr)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
   });
   return g_encode ? LMCE_OK : fail(LMCE_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
 }
@@ -140,8 +149,7 @@ int launch_engine(const CUtensorMap& ma, const CUtensorMap& mb, const EnginePara
     attr_done[dev] = true;
   }
   kern<<<grid, NUM_THREADS, smem, st>>>(ma, mb, p);
-  LMCE_CUDA(cudaGetLastError());
-  return LMCE_OK;
+  return launched();
 }
 
 template <int KIND, bool A_MN, bool B_MN>
@@ -526,8 +534,7 @@ int lmce_stats_reduce(const lmce_part* parts, int64_t n_parts, int64_t tok_strid
       reinterpret_cast<const Part*>(parts), static_cast<int>(n_parts), tok_stride, part_stride,
       static_cast<int>(n_tokens), reinterpret_cast<Part*>(record_out), nullptr, nullptr, nullptr, nullptr, nullptr,
       d->err_ptr);
-  LMCE_CUDA(cudaGetLastError());
-  return LMCE_OK;
+  return launched();
 }
 
 int lmce_stats_finish(const lmce_part* parts, int64_t n_parts, int64_t tok_stride, int64_t part_stride,
@@ -545,11 +552,10 @@ int lmce_stats_finish(const lmce_part* parts, int64_t n_parts, int64_t tok_strid
   stats_merge_kernel<true><<<static_cast<int>(blocks), warps * 32, 0, st>>>(
       reinterpret_cast<const Part*>(parts), static_cast<int>(n_parts), tok_stride, part_stride,
       static_cast<int>(n_tokens), nullptr, labels, lse, nll, entropy, argmax, d->err_ptr);
-  LMCE_CUDA(cudaGetLastError());
+  if (int rc = launched()) return rc;
   loss_kernel<<<1, 1024, 0, st>>>(nll, labels, static_cast<int>(n_tokens), num_items_dev,
                                   static_cast<float>(num_items), loss, denom);
-  LMCE_CUDA(cudaGetLastError());
-  return LMCE_OK;
+  return launched();
 }
 
 size_t lmce_bwd_workspace_bytes(int64_t n_tokens, int64_t hidden_dim, int64_t vocab_local, int64_t v_chunk) {
@@ -592,7 +598,7 @@ int lmce_backward(const void* hidden, const void* weight, const int64_t* labels,
   if (d_hidden) LMCE_CUDA(cudaMemsetAsync(d_hidden, 0, 2ull * n * h, st));
 
   compact_kernel<<<1, 1024, 0, st>>>(labels, n, vocab_offset, vl, lse, count, row_idx, lbl_lab, lse_lab);
-  LMCE_CUDA(cudaGetLastError());
+  if (int rc = launched()) return rc;
   {
     const int vec = h * 2 / 16;
     const long long total = static_cast<long long>(L.rows_pad) * vec;
@@ -600,7 +606,7 @@ int lmce_backward(const void* hidden, const void* weight, const int64_t* labels,
     if (blocks > d->sms * 8ll) blocks = d->sms * 8ll;
     gather_rows_kernel<<<static_cast<int>(blocks), 256, 0, st>>>(static_cast<const uint4*>(hidden), vec, count,
                                                                  row_idx, L.rows_pad, static_cast<uint4*>(x_lab));
-    LMCE_CUDA(cudaGetLastError());
+    if (int rc = launched()) return rc;
   }
 
   const bool want_dx = d_hidden != nullptr || d_hidden_f32 != nullptr;
@@ -694,16 +700,16 @@ int lmce_dx_finalize(const float* d_hidden_f32, int64_t n_tokens, int64_t hidden
         reinterpret_cast<const float4*>(d_hidden_f32), n4, static_cast<uint2*>(d_hidden));
   else
     return fail(LMCE_ERR_UNSUPPORTED, "dtype %d", dtype);
-  LMCE_CUDA(cudaGetLastError());
-  return LMCE_OK;
+  return launched();
 }
 
 int lmce_selftest_wait_timeout(uint64_t timeout_ns, void* stream) {
   DevInfo* d = nullptr;
   if (int rc = device_info(&d)) return rc;
   selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(timeout_ns, d->err_ptr);
-  LMCE_CUDA(cudaGetLastError());
-  return LMCE_OK;
+  return launched();
 }
+
+uint64_t lmce_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 }  // extern "C"
