@@ -130,6 +130,34 @@ LMCE_API int lmce_backward(const void* hidden, const void* weight, const int64_t
 LMCE_API int lmce_dx_finalize(const float* d_hidden_f32, int64_t n_tokens, int64_t hidden_dim, int dtype,
                      void* d_hidden, void* stream);
 
+/* ----------------------------------------------- no-allocation forward */
+
+/* Bytes of the library's fixed device scratch used by lmce_forward_noalloc. */
+#define LMCE_NOALLOC_SCRATCH_BYTES (8u << 20)
+
+/* Forward (statistics + finish) that allocates nothing. No counterpart in the
+ * reference: it exists for callers that cannot allocate device memory
+ * themselves — plugins inside a runtime that owns every device allocation,
+ * foreign-language bindings that can only pass tensor pointers, and serving
+ * loops that forbid allocation after warm-up because an allocation can stall
+ * the device. Such callers pass only the inputs and outputs of
+ * lmce_fwd_stats + lmce_stats_finish; the per-token partial records live in
+ * a file-scope device array of LMCE_NOALLOC_SCRATCH_BYTES (8 MiB) inside this
+ * library, held by every GPU that loads the library until the process exits.
+ *   limit: n_tokens <= LMCE_NOALLOC_SCRATCH_BYTES / sizeof(lmce_part)
+ *          (349525 tokens); larger n_tokens returns LMCE_ERR_INVALID_ARGUMENT.
+ * The first call on a device looks up the array's device address (once per
+ * device, with that device current); make that first call before any stream
+ * capture. All calls share the one array and it keeps the last call's
+ * contents: calls that overlap on the GPU (other streams, other host threads)
+ * race on it and must be serialised by the caller. Nothing in it needs to
+ * start at zero: every record the finish step reads is written earlier in the
+ * same call. Outputs and semantics are those of lmce_stats_finish. */
+LMCE_API int lmce_forward_noalloc(const void* hidden, const void* weight, const int64_t* labels, int64_t n_tokens,
+                                  int64_t hidden_dim, int64_t vocab, int dtype, const float* num_items_dev,
+                                  double num_items, float* lse, float* nll, float* entropy, int64_t* argmax,
+                                  float* loss, float* denom, void* stream);
+
 /* ------------------------------------------------------------ diagnostics */
 
 /* Number of kernels this library has launched in this process (all devices). */

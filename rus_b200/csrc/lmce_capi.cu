@@ -713,3 +713,63 @@ int lmce_selftest_wait_timeout(uint64_t timeout_ns, void* stream) {
 uint64_t lmce_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 }  // extern "C"
+
+// ======================================================= no-allocation forward ===
+//
+// Scratch for lmce_forward_noalloc: a fixed device array inside this library, so
+// a caller that cannot allocate device memory can still run the forward. Host
+// code never passes the symbol itself to a kernel (on the host it names a
+// stand-in, not device memory); it looks up the device address once per device
+// with cudaGetSymbolAddress and passes that pointer.
+
+static __device__ __align__(256) unsigned char g_lmce_noalloc_scratch[LMCE_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+void* g_noalloc_ptr[kMaxDevices] = {};
+std::mutex g_noalloc_mu;
+
+// Device address of the scratch array on the current device (looked up on the first call per device).
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  LMCE_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return fail(LMCE_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_lmce_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(LMCE_ERR_CUDA, "cudaGetSymbolAddress(no-allocation scratch) failed: %s", cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return LMCE_OK;
+}
+
+}  // namespace
+
+extern "C" int lmce_forward_noalloc(const void* hidden, const void* weight, const int64_t* labels, int64_t n_tokens,
+                                    int64_t hidden_dim, int64_t vocab, int dtype, const float* num_items_dev,
+                                    double num_items, float* lse, float* nll, float* entropy, int64_t* argmax,
+                                    float* loss, float* denom, void* stream) {
+  constexpr int64_t kMaxRecords = static_cast<int64_t>(LMCE_NOALLOC_SCRATCH_BYTES / sizeof(lmce_part));
+  if (n_tokens <= 0) return fail(LMCE_ERR_INVALID_ARGUMENT, "bad n_tokens %lld", (long long)n_tokens);
+  if (n_tokens > kMaxRecords)
+    return fail(LMCE_ERR_INVALID_ARGUMENT,
+                "n_tokens %lld exceeds the no-allocation scratch: %u bytes hold at most %lld tokens "
+                "(use lmce_fwd_stats with a caller-allocated buffer)",
+                (long long)n_tokens, LMCE_NOALLOC_SCRATCH_BYTES, (long long)kMaxRecords);
+  if (vocab <= 0) return fail(LMCE_ERR_INVALID_ARGUMENT, "bad vocab size");
+  // vocab slabs per token block, capped so n_tokens x slabs records fit the scratch
+  int64_t parts = lmce_fwd_num_parts(n_tokens, vocab);
+  const int64_t cap = kMaxRecords / n_tokens;
+  if (parts > cap) parts = cap;
+  if (parts < 1) parts = 1;
+  void* scratch = nullptr;
+  if (int rc = noalloc_scratch(&scratch)) return rc;
+  lmce_part* recs = static_cast<lmce_part*>(scratch);
+  if (int rc = lmce_fwd_stats(hidden, weight, labels, n_tokens, hidden_dim, vocab, 0, dtype, recs, parts, stream))
+    return rc;
+  return lmce_stats_finish(recs, parts, parts, 1, labels, n_tokens, num_items_dev, num_items, lse, nll, entropy,
+                           argmax, loss, denom, stream);
+}
