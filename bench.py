@@ -20,6 +20,7 @@ rank 0 runs it.
 from __future__ import annotations
 
 import argparse
+import faulthandler
 import json
 import math
 import os
@@ -43,6 +44,8 @@ PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # DRAM bytes (read + write) of one forward-statistics launch at config 2, from
 # one `ncu --set full` capture (profiles/lmce_head_c2_fwd_bwd.md).
 FWD_STATS_TRAFFIC_C2 = 499_676_416 + 5_951_744
+# DRAM bytes of one persistent backward launch at config 2 (same profile file); None until captured.
+BWD_TRAFFIC_C2 = None
 
 
 def load_peaks():
@@ -97,11 +100,18 @@ class ClockSampler:
             import pynvml
 
             pynvml.nvmlInit()
+            # match the CUDA device to its NVML handle by PCI domain / bus / device numbers
+            props = torch.cuda.get_device_properties(self.device)
+            want = (int(getattr(props, "pci_domain_id", -1)), int(getattr(props, "pci_bus_id", -1)),
+                    int(getattr(props, "pci_device_id", -1)))
             h = None
-            try:
-                bus = torch.cuda.get_device_properties(self.device).pci_bus_id
-                h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
-            except Exception:
+            for i in range(pynvml.nvmlDeviceGetCount()):
+                cand = pynvml.nvmlDeviceGetHandleByIndex(i)
+                pci = pynvml.nvmlDeviceGetPciInfo(cand)
+                if (int(pci.domain), int(pci.bus), int(pci.device)) == want:
+                    h = cand
+                    break
+            if h is None:
                 h = pynvml.nvmlDeviceGetHandleByIndex(self.device.index or 0)
             self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
         except Exception:
@@ -191,7 +201,12 @@ def workload_name(cfg):
 
 # ------------------------------------------------------------------ GPU side
 
+def stage(msg):
+    print(f"[bench] {msg}", file=sys.stderr, flush=True)
+
+
 def main():
+    faulthandler.enable()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
@@ -257,10 +272,12 @@ def main():
         torch.cuda.synchronize()
 
     # ---- warm-up
+    stage("warm-up")
     for _ in range(args.warmup):
         step()
     barrier()
 
+    stage("peak memory")
     # ---- peak activation memory of one step (beyond inputs and the dX/dW outputs)
     Xg.grad = None
     W.grad = None
@@ -273,19 +290,34 @@ def main():
     out_bytes = Xg.grad.numel() * Xg.grad.element_size() + W.grad.numel() * W.grad.element_size()
     peak_act_mib = max(peak - out_bytes, 0) / 2**20
 
-    # ---- device-timed steps (inputs resident in HBM; L2 flushed between steps)
+    # ---- device-timed steps (inputs resident in HBM; L2 flushed between steps). The two
+    # tensor-core kernels of each step are also bracketed by events recorded by the library
+    # (lmce_set_timing_events) on the launching stream.
+    def new_event():
+        e = torch.cuda.Event(enable_timing=True)
+        e.record(stream)  # create the underlying CUDA event before handing it to the library
+        return e
+
+    stage("timed steps")
     l0 = _lib.launch_count()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    kev = {k: [(new_event(), new_event()) for _ in range(args.steps)] for k in (0, 1)}
+    torch.cuda.synchronize()
     barrier()
     with ClockSampler(device) as clk:
         for i in range(args.steps):
             flush.zero_()
+            for k in (0, 1):
+                _lib.call("lmce_set_timing_events", k, kev[k][i][0].cuda_event, kev[k][i][1].cuda_event)
             ev[i][0].record(stream)
             step()
             ev[i][1].record(stream)
         barrier()
+    for k in (0, 1):
+        _lib.call("lmce_set_timing_events", k, None, None)
     launches = _lib.launch_count() - l0
     step_ms = [a.elapsed_time(b) for a, b in ev]
+    kern_ms = {k: statistics.mean(a.elapsed_time(b) for a, b in kev[k]) for k in (0, 1)}
     total_ms = torch.tensor([sum(step_ms)], dtype=torch.float64, device=device)
     if world > 1:
         dist.all_reduce(total_ms, op=dist.ReduceOp.MAX)
@@ -293,6 +325,7 @@ def main():
     tokens_per_step = n_tokens
     value = tokens_per_step / (ms_per_step / 1e3)
 
+    stage("end-to-end")
     # ---- end-to-end through the public API: pinned host inputs -> H2D, fwd+bwd, loss D2H
     Xh = X.cpu().pin_memory()
     yh = y.cpu().pin_memory()
@@ -322,29 +355,29 @@ def main():
     e2e_value = tokens_per_step / (e2e_ms_step / 1e3)
     h2d = Xh.numel() * Xh.element_size() + yh.numel() * yh.element_size()
 
-    # ---- roofline of the dominant kernel: the fused logits GEMM + statistics launch, timed alone
-    from rus_b200.ops import head_forward_stats
-
-    h2d_x = X.view(-1, H)
-    for _ in range(3):
-        head_forward_stats(h2d_x, W.detach(), y, v_lo)
-    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(10)]
-    for a, b in kev:
-        flush.zero_()
-        a.record(stream)
-        head_forward_stats(h2d_x, W.detach(), y, v_lo)
-        b.record(stream)
-    torch.cuda.synchronize()
-    k_ms = statistics.mean(a.elapsed_time(b) for a, b in kev)
+    stage("report")
+    # ---- roofline of the dominant kernel (largest share of the step)
     peaks, peak_kind = load_peaks()
     v_local = v_hi - v_lo
-    k_flops = 2.0 * n_tokens * H * v_local
-    k_achieved = k_flops / (k_ms / 1e3) / 1e12
     k_peak = float(peaks["bf16_tflops"])
+    sust = float(peaks.get("bf16_tflops_sustained", k_peak))
+    kernels = {
+        "stats": {"name": "lmce_stats_kernel (fused logits GEMM + online softmax statistics)",
+                  "ms": kern_ms[0], "alg_flops": 2.0 * n_tokens * H * v_local,
+                  "exec_flops": 2.0 * n_tokens * H * v_local, "traffic": FWD_STATS_TRAFFIC_C2},
+        "backward": {"name": "lmce_bwd_kernel (persistent: recomputed logits -> G, dX and dW GEMMs)",
+                     "ms": kern_ms[1], "alg_flops": 4.0 * n_lab * H * v_local,
+                     "exec_flops": 6.0 * n_lab * H * v_local, "traffic": BWD_TRAFFIC_C2},
+    }
+    for kk in kernels.values():
+        kk["achieved_tflops"] = kk["alg_flops"] / (kk["ms"] / 1e3) / 1e12
+        kk["executed_tflops"] = kk["exec_flops"] / (kk["ms"] / 1e3) / 1e12
+        kk["share_of_step"] = kk["ms"] / ms_per_step
+    dom_key = max(kernels, key=lambda k: kernels[k]["ms"])
+    dom = kernels[dom_key]
     # whole-step roofline: algorithmic flops 2*N*H*V + 4*N_lab*H*V (recompute not credited)
     step_flops = 2.0 * n_tokens * H * v_local + 4.0 * n_lab * H * v_local
     step_tflops = step_flops / (ms_per_step / 1e3) / 1e12
-    sust = float(peaks.get("bf16_tflops_sustained", k_peak))
 
     if world > 1:
         dist.barrier(device_ids=[local_rank])
@@ -392,13 +425,16 @@ def main():
             "gpu_launches": int(launches),
             "roofline": {
                 "bound": "tensor",
-                "kernel": "lmce_gemm_kernel<STATS> (fused logits GEMM + online softmax stats)",
-                "achieved": k_achieved, "peak": k_peak, "unit": "TFLOP/s", "frac": k_achieved / k_peak,
+                "kernel": dom["name"],
+                "achieved": dom["achieved_tflops"], "peak": k_peak, "unit": "TFLOP/s",
+                "frac": dom["achieved_tflops"] / k_peak,
                 "peak_kind": f"{peak_kind} burst bf16 (MEASURED_PEAKS.json)",
-                "traffic": FWD_STATS_TRAFFIC_C2 if (args.config == "c2" and world == 1) else None,
-                "launch_ms": k_ms, "flops_per_launch": k_flops,
+                "traffic": dom["traffic"] if (args.config == "c2" and world == 1) else None,
+                "launch_ms": dom["ms"], "flops_per_launch": dom["alg_flops"],
+                "executed_tflops": dom["executed_tflops"],
                 "step_frac_of_sustained": step_tflops / sust,
             },
+            "kernels": {k: {kk: v for kk, v in d.items() if kk != "name"} for k, d in kernels.items()},
             "clocks": clk.summary(),
             "device_error": err,
         }

@@ -163,6 +163,14 @@ LMCE_API int lmce_forward_noalloc(const void* hidden, const void* weight, const 
 /* Number of kernels this library has launched in this process (all devices). */
 LMCE_API uint64_t lmce_launch_count(void);
 
+/* Timing hook for benchmarks: process-wide, record the CUDA events
+ * `begin` and `end` (cudaEvent_t passed as void*) on the call's stream right
+ * before and after the main tensor-core kernel of later calls:
+ *   which = 0: the statistics kernel of lmce_fwd_stats
+ *   which = 1: the persistent kernel of lmce_backward
+ * NULL events switch recording off. The events must already exist. */
+LMCE_API int lmce_set_timing_events(int which, void* begin, void* end);
+
 /* Launches a kernel whose bounded wait is never satisfied; after timeout_ns it
  * records LMCE_ERR_TIMEOUT in the device error word and returns normally.
  * Exercises the failure path without hanging or faulting the GPU. */

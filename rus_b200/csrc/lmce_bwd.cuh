@@ -1,0 +1,560 @@
+// Persistent backward of the lm_head CE head: one launch computes dX and dW.
+//
+// The vocabulary is cut into chunks of v_chunk rows. For chunk c three kinds of
+// 128x256 output tiles exist:
+//   G(c)   recomputed logits tile X_lab . W_c^T -> G = (softmax - onehot) * 2^15
+//          in the input dtype, written to G buffer c % NUM_GBUF
+//          (replaces the reference's pass-2 GEMM + lm_head_piece_kernel MODE 1,
+//          solution/ops.py:287-319, solution/kernels.py:517-531)
+//   DX(c)  dX_tile += G_c . W_c (K = chunk width); fp32 accumulation across chunks
+//          in chunk order; the last chunk scales by grad_loss / denom / 2^15 and
+//          scatters rows to token order (replaces ops.py:320 and 337-338)
+//   DW(c)  dW rows of chunk c = G_c^T . X_lab (K = labelled tokens); new, the
+//          reference returns None for the weight (ops.py:339)
+// All tiles of the whole backward form one list, claimed in order through an
+// atomic ticket by persistent CTAs (one per SM):
+//   G(0) G(1) DX(0) DW(0) G(2) DX(1) DW(1) ... G(C-1) DX(C-2) DW(C-2) DX(C-1) DW(C-1)
+// with device-side dependencies checked by the TMA producer before it loads a tile:
+//   DX(c), DW(c) wait for all G(c) tiles (gdone[c]);
+//   G(c) waits until the DX/DW tiles of chunk c - NUM_GBUF released its buffer (consumed[]);
+//   DX(c) tile (m,n) waits for DX(c-1) tile (m,n) (dxchain[]), keeping the fp32
+//   read-modify-write of dX in chunk order (deterministic, no atomics on data).
+// A tile only waits for tiles earlier in the list, and tiles are claimed in list
+// order by running CTAs, so the earliest unfinished tile can always progress.
+// Producers of a dependency publish with stores -> CTA barrier -> fence ->
+// atomic add; consumers acquire the counter, then fence the async proxy before
+// their TMA reads of G. Every wait is bounded.
+#pragma once
+
+#include "lmce_engine.cuh"
+
+namespace lmce {
+
+constexpr int NUM_GBUF = 3;
+constexpr int SCHED_DEPTH = 4;
+
+enum : int { BK_END = -1, BK_G = 0, BK_DX = 1, BK_DW = 2 };
+
+struct BwdTile {
+  int kind, chunk, m, n;
+};
+
+struct BwdParams {
+  int rows_pad;            // allocated rows of X_lab and of each G buffer (multiple of 128)
+  int H;                   // hidden size
+  int V;                   // vocab rows of this shard
+  int v_chunk;             // chunk width (multiple of 256)
+  int n_chunks;
+  const int* count;        // device: number of labelled tokens (compacted rows)
+  const int* lbl_lab;      // per compacted row: label local to the shard, -1 if elsewhere
+  const float* lse_lab;    // per compacted row: lse
+  void* g;                 // G buffers [NUM_GBUF][rows_pad][v_chunk], input dtype
+  float* dx_acc;           // fp32 [rows_pad][H], compacted row order
+  const int* row_idx;      // compacted row -> token row
+  void* dx_out;            // [N][H] input dtype (nullable)
+  float* dx_out_f32;       // [N][H] fp32 (nullable; vocab-sharded runs)
+  void* dw_out;            // [V][H] input dtype (nullable)
+  int want_dx, want_dw;
+  const float* grad_loss;  // device scalar (nullable: 1)
+  const float* denom;      // device scalar
+  float gscale;            // G prescale
+  int* sync;               // zeroed: [0] ticket, [1..C] gdone, [1+C..2C] consumed, [1+2C..] dxchain
+  int* err;
+  unsigned long long timeout_ns;
+};
+
+// Geometry derived from the parameters and the device-side labelled-token count
+// (identical in every thread of every CTA).
+struct BwdGeom {
+  int n_lab, num_m, num_hn, C, vc, V;
+  bool dx, dw;
+  __device__ __forceinline__ int width(int c) const { return min(vc, V - c * vc); }
+  __device__ __forceinline__ int nG(int c) const { return num_m * ((width(c) + BN - 1) / BN); }
+  __device__ __forceinline__ int nDX() const { return dx ? num_m * num_hn : 0; }
+  __device__ __forceinline__ int nDW(int c) const { return dw ? ((width(c) + BM - 1) / BM) * num_hn : 0; }
+  __device__ __forceinline__ int num_kb(const BwdTile& t, int H) const {
+    if (t.kind == BK_G) return (H + BK - 1) / BK;
+    if (t.kind == BK_DX) return (width(t.chunk) + BK - 1) / BK;
+    return (n_lab + BK - 1) / BK;
+  }
+};
+
+__device__ __forceinline__ BwdGeom make_geom(const BwdParams& p) {
+  BwdGeom g;
+  g.n_lab = *p.count;
+  g.num_m = (g.n_lab + BM - 1) / BM;
+  g.num_hn = (p.H + BN - 1) / BN;
+  g.C = p.n_chunks;
+  g.vc = p.v_chunk;
+  g.V = p.V;
+  g.dx = p.want_dx != 0;
+  g.dw = p.want_dw != 0;
+  return g;
+}
+
+// Decoder of the tile list (see the file comment). Segments are walked with a
+// forward-only cursor: one producer thread asks for increasing ticket numbers,
+// so the total walking over a launch is one pass over the ~3C segments.
+struct TileCursor {
+  int seg;             // segment index: 0 = G(0); then 3 per chunk c: G(c+1), DX(c), DW(c)
+  long long seg_start; // first ticket of segment `seg`
+
+  __device__ __forceinline__ void init() {
+    seg = 0;
+    seg_start = 0;
+  }
+
+  // kind, chunk, count and m-extent of segment `s`; false past the last segment
+  __device__ __forceinline__ static bool segment(const BwdGeom& g, int s, int& kind, int& chunk, int& count,
+                                                 int& mdim) {
+    if (s == 0) {
+      kind = BK_G;
+      chunk = 0;
+      count = g.nG(0);
+      mdim = g.num_m;
+      return true;
+    }
+    const int c = (s - 1) / 3, r = (s - 1) % 3;
+    if (c >= g.C) return false;
+    if (r == 0) {
+      kind = BK_G;
+      chunk = c + 1;
+      count = c + 1 < g.C ? g.nG(c + 1) : 0;
+      mdim = g.num_m;
+    } else if (r == 1) {
+      kind = BK_DX;
+      chunk = c;
+      count = g.nDX();
+      mdim = g.num_m;
+    } else {
+      kind = BK_DW;
+      chunk = c;
+      count = g.nDW(c);
+      mdim = (g.width(c) + BM - 1) / BM;
+    }
+    return true;
+  }
+
+  // Tile of ticket t (t never decreases between calls); false past the end of the list.
+  __device__ __forceinline__ bool decode(const BwdGeom& g, long long t, BwdTile& out) {
+    for (;;) {
+      int kind, chunk, count, mdim;
+      if (!segment(g, seg, kind, chunk, count, mdim)) return false;
+      if (t < seg_start + count) {
+        const int i = static_cast<int>(t - seg_start);
+        out.kind = kind;
+        out.chunk = chunk;
+        out.m = i % mdim;
+        out.n = i / mdim;
+        return true;
+      }
+      seg_start += count;
+      ++seg;
+    }
+  }
+};
+
+// Read a schedule-ring entry written by the producer thread (after the sched_full wait).
+__device__ __forceinline__ BwdTile read_ring(const BwdTile* e) {
+  const volatile int* v = reinterpret_cast<const volatile int*>(e);
+  BwdTile t;
+  t.kind = v[0];
+  t.chunk = v[1];
+  t.m = v[2];
+  t.n = v[3];
+  return t;
+}
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Bounded wait until *p >= target (acquire). False on timeout or abort.
+__device__ __forceinline__ bool wait_counter(const int* p, int target, volatile int* abort, uint64_t limit_ns) {
+  if (ld_acquire_gpu(p) >= target) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (;;) {
+    __nanosleep(128);
+    if (ld_acquire_gpu(p) >= target) return true;
+    if (*abort) return false;
+    if (global_timer_ns() - t0 > limit_ns) return false;
+  }
+}
+
+// Publish: all 128 epilogue threads' global stores happen before the increment.
+__device__ __forceinline__ void publish_add(int* ctr, int v) {
+  epilogue_bar();
+  if (threadIdx.x == EPI_THREAD0) {
+    __threadfence();
+    atomicAdd(ctr, v);
+  }
+}
+
+template <bool BF16, int STAGES>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    lmce_bwd_kernel(const __grid_constant__ CUtensorMap map_xk, const __grid_constant__ CUtensorMap map_xmn,
+                    const __grid_constant__ CUtensorMap map_wk, const __grid_constant__ CUtensorMap map_wmn,
+                    const __grid_constant__ CUtensorMap map_gk, const __grid_constant__ CUtensorMap map_gmn,
+                    const BwdParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint64_t* drain_bar = tempty_bar + 2;
+  uint64_t* sched_full = drain_bar + 1;
+  uint64_t* sched_empty = sched_full + SCHED_DEPTH;
+  BwdTile* ring = reinterpret_cast<BwdTile*>(sched_empty + SCHED_DEPTH);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(ring + SCHED_DEPTH);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = __shfl_sync(0xffffffffu, threadIdx.x / 32, 0);
+  const int lane = threadIdx.x & 31;
+  const BwdGeom geo = make_geom(p);
+  int* ticket = p.sync;
+  int* gdone = p.sync + 1;
+  int* consumed = p.sync + 1 + p.n_chunks;
+  int* dxchain = p.sync + 1 + 2 * p.n_chunks;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull_bar[b], 1);
+      mbar_init(&tempty_bar[b], EPI_THREADS);
+    }
+    mbar_init(drain_bar, 1);
+    for (int s = 0; s < SCHED_DEPTH; ++s) {
+      mbar_init(&sched_full[s], 1);
+      mbar_init(&sched_empty[s], 1 + EPI_THREADS);  // UMMA lane + epilogue threads
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&map_xk);
+    tma_prefetch_desc(&map_xmn);
+    tma_prefetch_desc(&map_wk);
+    tma_prefetch_desc(&map_wmn);
+    tma_prefetch_desc(&map_gk);
+    tma_prefetch_desc(&map_gmn);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  const uint64_t tlimit = p.timeout_ns;
+
+  if (warp == 0) {
+    // ------------------------------------------- scheduler + TMA producer ---
+    if (lane == 0) {
+      int stage = 0, slot = 0;
+      uint32_t phase = 0, sphase = 0;
+      int issued = 0;
+      bool ok = true;
+      TileCursor cur;
+      cur.init();
+      int next_ticket = atomicAdd(ticket, 1);  // claimed one tile ahead of its loads
+      for (;;) {
+        if (!mbar_wait(&sched_empty[slot], sphase ^ 1u, abort_flag, tlimit)) {
+          ok = false;
+          break;
+        }
+        BwdTile t;
+        const bool has = cur.decode(geo, next_ticket, t);
+        if (!has) t.kind = BK_END;
+        {
+          volatile int* e = reinterpret_cast<volatile int*>(&ring[slot]);
+          e[0] = t.kind;
+          e[1] = t.chunk;
+          e[2] = t.m;
+          e[3] = t.n;
+        }
+        mbar_arrive(&sched_full[slot]);
+        if (++slot == SCHED_DEPTH) {
+          slot = 0;
+          sphase ^= 1u;
+        }
+        if (!has) break;
+        next_ticket = atomicAdd(ticket, 1);  // result is first needed after this tile's loads
+
+        // dependencies of this tile
+        const int gbuf = t.chunk % NUM_GBUF;
+        if (t.kind == BK_G) {
+          if (t.chunk >= NUM_GBUF) {
+            const int prev = t.chunk - NUM_GBUF;
+            ok = wait_counter(&consumed[prev], geo.nDX() + geo.nDW(prev), abort_flag, tlimit);
+          }
+        } else {
+          ok = wait_counter(&gdone[t.chunk], geo.nG(t.chunk), abort_flag, tlimit);
+          if (ok && t.kind == BK_DX && t.chunk > 0)
+            ok = wait_counter(&dxchain[t.m * geo.num_hn + t.n], t.chunk, abort_flag, tlimit);
+          asm volatile("fence.proxy.async.global;" ::: "memory");  // G was written by generic stores
+        }
+        if (!ok) break;
+
+        const int nkb = geo.num_kb(t, p.H);
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, tlimit)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + stage * STAGE_BYTES;
+          uint8_t* sb = sa + A_BYTES;
+          uint64_t* fb = &full_bar[stage];
+          mbar_arrive_expect_tx(fb, STAGE_BYTES);
+          const int k0 = kb * BK;
+          if (t.kind == BK_G) {
+            load_operand<BM>(sa, &map_xk, fb, false, t.m * BM, k0);
+            load_operand<BN>(sb, &map_wk, fb, false, t.chunk * p.v_chunk + t.n * BN, k0);
+          } else if (t.kind == BK_DX) {
+            load_operand<BM>(sa, &map_gk, fb, false, gbuf * p.rows_pad + t.m * BM, k0);
+            load_operand<BN>(sb, &map_wmn, fb, true, t.n * BN, t.chunk * p.v_chunk + k0);
+          } else {
+            load_operand<BM>(sa, &map_gmn, fb, true, t.m * BM, gbuf * p.rows_pad + k0);
+            load_operand<BN>(sb, &map_xmn, fb, true, t.n * BN, k0);
+          }
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+      }
+      if (!ok) {
+        raise_error(p.err, ERR_TIMEOUT);
+        *abort_flag = 1;
+        const int outstanding = issued < STAGES ? issued : STAGES;
+        for (int i = 1; i <= outstanding; ++i) {
+          int s = stage - i;
+          uint32_t ph = phase;
+          if (s < 0) {
+            s += STAGES;
+            ph ^= 1u;
+          }
+          volatile int no_abort = 0;
+          mbar_wait(&full_bar[s], ph, &no_abort, tlimit);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // -------------------------------------------------------- UMMA issuer ---
+    if (lane == 0) {
+      int stage = 0, slot = 0, acc = 0;
+      uint32_t phase = 0, sphase = 0, acc_phase = 0;
+      bool ok = true;
+      for (;;) {
+        if (!mbar_wait(&sched_full[slot], sphase, abort_flag, tlimit)) {
+          ok = false;
+          break;
+        }
+        const BwdTile t = read_ring(&ring[slot]);
+        mbar_arrive(&sched_empty[slot]);
+        if (++slot == SCHED_DEPTH) {
+          slot = 0;
+          sphase ^= 1u;
+        }
+        if (t.kind == BK_END) break;
+        const bool a_mn = t.kind == BK_DW;
+        const bool b_mn = t.kind != BK_G;
+        const uint32_t idesc = make_idesc_f16(BF16, a_mn, b_mn, BM, BN);
+        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, abort_flag, tlimit)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        const int nkb = geo.num_kb(t, p.H);
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, abort_flag, tlimit)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / UMMA_K; ++k)
+            umma_f16_ss(d_tmem, operand_desc(sa, a_mn, k), operand_desc(sa + A_BYTES, b_mn, k), idesc,
+                        (kb | k) != 0 ? 1u : 0u);
+          umma_commit(&empty_bar[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull_bar[acc]);  // also fires when nkb == 0 (no UMMA issued)
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      if (!ok) {
+        raise_error(p.err, ERR_TIMEOUT);
+        *abort_flag = 1;
+      }
+      umma_commit(drain_bar);
+      volatile int no_abort = 0;
+      mbar_wait(drain_bar, 0, &no_abort, tlimit);
+    }
+  } else {
+    // ---------------------------------------------------------- epilogue ---
+    const int q = warp & 3;
+    const int r_in_tile = q * 32 + lane;
+    const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+    const float gl = p.grad_loss ? *p.grad_loss : 1.0f;
+    const float dscale = gl / (*p.denom) / p.gscale;
+    int slot = 0, acc = 0;
+    uint32_t sphase = 0, acc_phase = 0;
+    bool ok = true;
+    for (;;) {
+      if (!mbar_wait(&sched_full[slot], sphase, abort_flag, tlimit)) {
+        ok = false;
+        break;
+      }
+      const BwdTile t = read_ring(&ring[slot]);
+      mbar_arrive(&sched_empty[slot]);
+      if (++slot == SCHED_DEPTH) {
+        slot = 0;
+        sphase ^= 1u;
+      }
+      if (t.kind == BK_END) break;
+      const bool have_acc = geo.num_kb(t, p.H) > 0;
+      const int w = geo.width(t.chunk);
+      const int row = t.m * BM + r_in_tile;
+
+      // per-row inputs of a G tile
+      int lbl = -1;
+      float lseL = 0.f;
+      const bool g_row_ok = row < geo.n_lab;
+      if (t.kind == BK_G && g_row_ok) {
+        const int y = p.lbl_lab[row];
+        lbl = y >= 0 ? y - t.chunk * p.v_chunk : -1;
+        lseL = p.lse_lab[row] * LOG2E;
+      }
+      if (t.kind == BK_DX && t.chunk > 0) {
+        // dX rows of this tile were last written by DX(chunk-1) on some CTA.
+        if (threadIdx.x == EPI_THREAD0 &&
+            !wait_counter(&dxchain[t.m * geo.num_hn + t.n], t.chunk, abort_flag, tlimit)) {
+          raise_error(p.err, ERR_TIMEOUT);
+          *abort_flag = 1;
+        }
+        epilogue_bar();
+      }
+      if (!mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, tlimit)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + lane_base + static_cast<uint32_t>(acc * BN);
+
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t raw[32];
+        float v[32];
+        __syncwarp();
+        tmem_ld_32x32b_x32(taddr + c * 32, raw);
+        tmem_ld_wait(raw);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = have_acc ? __uint_as_float(raw[j]) : 0.0f;
+        const int col0 = t.n * BN + c * 32;
+
+        if (t.kind == BK_G) {
+          // G = (softmax - onehot) * 2^15 on the dtype-rounded logits; 0 outside the chunk / labelled rows
+          const unsigned rel = static_cast<unsigned>(lbl - col0);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float z = round_to_input<BF16>(v[j]);
+            float pr = ex2_approx(fmaf(z, LOG2E, -lseL));
+            if (static_cast<unsigned>(j) == rel) pr -= 1.0f;
+            v[j] = (g_row_ok && col0 + j < w) ? pr * p.gscale : 0.0f;
+          }
+          char* dst = reinterpret_cast<char*>(p.g) +
+                      ((static_cast<size_t>(t.chunk % NUM_GBUF) * p.rows_pad + row) * p.v_chunk + col0) * 2;
+          store32_dtype<BF16>(dst, v);
+        } else if (t.kind == BK_DX) {
+          if (row < geo.n_lab && col0 < p.H) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] *= dscale;
+            float* accp = p.dx_acc + static_cast<size_t>(row) * p.H + col0;
+            if (t.chunk > 0) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4) {
+                const float4 a4 = __ldcg(reinterpret_cast<const float4*>(accp + j));
+                v[j] += a4.x;
+                v[j + 1] += a4.y;
+                v[j + 2] += a4.z;
+                v[j + 3] += a4.w;
+              }
+            }
+            if (t.chunk + 1 < geo.C) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4)
+                __stcg(reinterpret_cast<float4*>(accp + j), make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
+            } else {
+              const size_t trow = static_cast<size_t>(p.row_idx[row]);
+              if (p.dx_out_f32 != nullptr) {
+                float* dst = p.dx_out_f32 + trow * p.H + col0;
+#pragma unroll
+                for (int j = 0; j < 32; j += 4)
+                  *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+              }
+              if (p.dx_out != nullptr) store32_dtype<BF16>(reinterpret_cast<char*>(p.dx_out) + (trow * p.H + col0) * 2, v);
+            }
+          }
+        } else {  // BK_DW
+          if (row < w && col0 < p.H) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] *= dscale;
+            char* dst = reinterpret_cast<char*>(p.dw_out) +
+                        ((static_cast<size_t>(t.chunk) * p.v_chunk + row) * p.H + col0) * 2;
+            store32_dtype<BF16>(dst, v);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty_bar[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+      // publish completion for dependent tiles
+      if (t.kind == BK_G) {
+        publish_add(&gdone[t.chunk], 1);
+      } else if (t.kind == BK_DX) {
+        epilogue_bar();
+        if (threadIdx.x == EPI_THREAD0) {
+          __threadfence();
+          atomicAdd(&dxchain[t.m * geo.num_hn + t.n], 1);
+          atomicAdd(&consumed[t.chunk], 1);
+        }
+      } else {
+        publish_add(&consumed[t.chunk], 1);
+      }
+    }
+    if (!ok) {
+      raise_error(p.err, ERR_TIMEOUT);
+      *abort_flag = 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+}  // namespace lmce

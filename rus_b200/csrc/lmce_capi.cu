@@ -14,7 +14,7 @@
 #include <mutex>
 
 #include "../../include/lmce.h"
-#include "lmce_engine.cuh"
+#include "lmce_bwd.cuh"
 
 using namespace lmce;
 
@@ -27,6 +27,17 @@ namespace {
 
 thread_local char t_err[512] = "";
 std::atomic<unsigned long long> g_launches{0};
+// Process-wide (not per thread): autograd runs backward passes on its own worker thread.
+std::atomic<CUevent> g_timing[2][2] = {{{nullptr}, {nullptr}}, {{nullptr}, {nullptr}}};
+PFN_cuEventRecord_v2000 g_event_record = nullptr;
+
+// Records the benchmark timing event of slot `which` (edge 0 begin / 1 end), if set.
+// The driver call is used because the events usually come from another runtime
+// instance in the process (the caller's framework); driver handles are shared.
+void timing_mark(int which, int edge, cudaStream_t st) {
+  CUevent ev = g_timing[which][edge].load(std::memory_order_acquire);
+  if (ev != nullptr && g_event_record != nullptr) g_event_record(ev, reinterpret_cast<CUstream>(st));
+}
 
 // Every kernel launch in this file goes through this check, which also counts it.
 int launched() {
@@ -131,32 +142,47 @@ int make_map(CUtensorMap* m, const void* base, bool bf16, uint64_t inner, uint64
   return LMCE_OK;
 }
 
-// ---------------------------------------------------------------- engine ---
+// ---------------------------------------------------------------- engines ---
 
-constexpr int kBN = 256;
+constexpr int kBN = BN;
 constexpr int kStages = 4;
 
-template <int KIND, bool A_MN, bool B_MN, bool BF16>
-int launch_engine(const CUtensorMap& ma, const CUtensorMap& mb, const EngineParams& p, int grid,
-                  cudaStream_t st) {
-  auto kern = lmce_gemm_kernel<KIND, kBN, A_MN, B_MN, BF16, kStages>;
-  constexpr int smem = engine_smem_bytes<kBN, kStages>();
-  static bool attr_done[kMaxDevices] = {};
+// Opt the kernel into its dynamic shared memory once per device.
+template <typename K>
+int ensure_smem_attr(K kern, int smem, bool* done) {
   int dev = 0;
   LMCE_CUDA(cudaGetDevice(&dev));
-  if (!attr_done[dev]) {
+  if (!done[dev]) {
     LMCE_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr_done[dev] = true;
+    done[dev] = true;
   }
-  kern<<<grid, NUM_THREADS, smem, st>>>(ma, mb, p);
-  return launched();
+  return LMCE_OK;
 }
 
-template <int KIND, bool A_MN, bool B_MN>
-int launch_engine_dt(bool bf16, const CUtensorMap& ma, const CUtensorMap& mb, const EngineParams& p, int grid,
-                     cudaStream_t st) {
-  return bf16 ? launch_engine<KIND, A_MN, B_MN, true>(ma, mb, p, grid, st)
-              : launch_engine<KIND, A_MN, B_MN, false>(ma, mb, p, grid, st);
+template <bool BF16>
+int launch_stats(const CUtensorMap& mx, const CUtensorMap& mw, const StatsParams& p, int grid, cudaStream_t st) {
+  auto kern = lmce_stats_kernel<BF16, kStages>;
+  constexpr int smem = engine_smem_bytes<kStages>();
+  static bool done[kMaxDevices] = {};
+  if (int rc = ensure_smem_attr(kern, smem, done)) return rc;
+  timing_mark(0, 0, st);
+  kern<<<grid, NUM_THREADS, smem, st>>>(mx, mw, p);
+  const int rc = launched();
+  timing_mark(0, 1, st);
+  return rc;
+}
+
+template <bool BF16>
+int launch_bwd(const CUtensorMap* maps, const BwdParams& p, int grid, cudaStream_t st) {
+  auto kern = lmce_bwd_kernel<BF16, kStages>;
+  constexpr int smem = engine_smem_bytes<kStages>();
+  static bool done[kMaxDevices] = {};
+  if (int rc = ensure_smem_attr(kern, smem, done)) return rc;
+  timing_mark(1, 0, st);
+  kern<<<grid, NUM_THREADS, smem, st>>>(maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], p);
+  const int rc = launched();
+  timing_mark(1, 1, st);
+  return rc;
 }
 
 // Vocab slabs per token block: fill the SMs with whole waves of (block, slab)
@@ -420,8 +446,8 @@ __global__ void selftest_wait_kernel(unsigned long long timeout_ns, int* err) {
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 struct BwdLayout {
-  size_t count, row_idx, lbl_lab, lse_lab, x_lab, g, dx_acc, total;
-  int rows_pad, v_chunk;
+  size_t count, row_idx, lbl_lab, lse_lab, x_lab, g, dx_acc, sync, total;
+  int rows_pad, v_chunk, n_chunks, sync_ints;
 };
 
 BwdLayout bwd_layout(int64_t n, int64_t h, int64_t v_local, int64_t v_chunk) {
@@ -432,7 +458,10 @@ BwdLayout bwd_layout(int64_t n, int64_t h, int64_t v_local, int64_t v_chunk) {
   if (vc > vmax) vc = vmax;
   if (vc < 256) vc = 256;
   L.v_chunk = static_cast<int>(vc);
+  L.n_chunks = static_cast<int>((v_local + vc - 1) / vc);
   L.rows_pad = static_cast<int>((n + BM - 1) / BM * BM);
+  const int num_hn = static_cast<int>((h + BN - 1) / BN);
+  L.sync_ints = 1 + 2 * L.n_chunks + (L.rows_pad / BM) * num_hn;
   size_t off = 0;
   L.count = off;
   off = align_up(off + 16, 256);
@@ -445,9 +474,11 @@ BwdLayout bwd_layout(int64_t n, int64_t h, int64_t v_local, int64_t v_chunk) {
   L.x_lab = off;
   off = align_up(off + 2ull * L.rows_pad * h, 256);
   L.g = off;
-  off = align_up(off + 2ull * L.rows_pad * vc, 256);
+  off = align_up(off + 2ull * NUM_GBUF * L.rows_pad * vc, 256);
   L.dx_acc = off;
   off = align_up(off + 4ull * L.rows_pad * h, 256);
+  L.sync = off;
+  off = align_up(off + sizeof(int) * L.sync_ints, 256);
   L.total = off;
   return L;
 }
@@ -503,15 +534,14 @@ int lmce_fwd_stats(const void* hidden, const void* weight, const int64_t* labels
   const int num_n = static_cast<int>((vocab_local + kBN - 1) / kBN);
   if (n_parts < 1 || n_parts > num_n) return fail(LMCE_ERR_INVALID_ARGUMENT, "n_parts %lld out of range", (long long)n_parts);
   const bool bf16 = dtype == LMCE_DTYPE_BF16;
-  CUtensorMap ma, mb;
-  if (int rc = make_map(&ma, hidden, bf16, hidden_dim, n_tokens, hidden_dim, BM)) return rc;
-  if (int rc = make_map(&mb, weight, bf16, hidden_dim, vocab_local, hidden_dim, kBN)) return rc;
-  EngineParams p{};
+  CUtensorMap mx, mw;
+  if (int rc = make_map(&mx, hidden, bf16, hidden_dim, n_tokens, hidden_dim, BM)) return rc;
+  if (int rc = make_map(&mw, weight, bf16, hidden_dim, vocab_local, hidden_dim, kBN)) return rc;
+  StatsParams p{};
   p.M = static_cast<int>(n_tokens);
   p.N = static_cast<int>(vocab_local);
   p.K = static_cast<int>(hidden_dim);
   p.n_slabs = static_cast<int>(n_parts);
-  p.v_limit = static_cast<int>(vocab_local);
   p.labels = labels;
   p.label_off = vocab_offset;
   p.parts = reinterpret_cast<Part*>(parts);
@@ -519,7 +549,8 @@ int lmce_fwd_stats(const void* hidden, const void* weight, const int64_t* labels
   p.timeout_ns = wait_timeout_ns();
   const long long units = static_cast<long long>(num_m) * n_parts;
   const int grid = static_cast<int>(units < d->sms ? units : d->sms);
-  return launch_engine_dt<KIND_STATS, false, false>(bf16, ma, mb, p, grid, static_cast<cudaStream_t>(stream));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return bf16 ? launch_stats<true>(mx, mw, p, grid, st) : launch_stats<false>(mx, mw, p, grid, st);
 }
 
 int lmce_stats_reduce(const lmce_part* parts, int64_t n_parts, int64_t tok_stride, int64_t part_stride,
@@ -613,71 +644,45 @@ int lmce_backward(const void* hidden, const void* weight, const int64_t* labels,
   const bool want_dw = d_weight != nullptr;
   if (!want_dx && !want_dw) return LMCE_OK;
 
-  // Tensor maps (chunk offsets are applied as TMA coordinates).
-  CUtensorMap m_xlab_k, m_w_k, m_g_k, m_w_mn, m_g_mn, m_xlab_mn;
-  if (int rc = make_map(&m_xlab_k, x_lab, bf16, h, L.rows_pad, h, BM)) return rc;
-  if (int rc = make_map(&m_w_k, weight, bf16, h, vl, h, kBN)) return rc;
-  if (int rc = make_map(&m_g_k, g, bf16, L.v_chunk, L.rows_pad, L.v_chunk, BM)) return rc;
-  if (int rc = make_map(&m_w_mn, weight, bf16, h, vl, h, 64)) return rc;
-  if (int rc = make_map(&m_g_mn, g, bf16, L.v_chunk, L.rows_pad, L.v_chunk, 64)) return rc;
-  if (int rc = make_map(&m_xlab_mn, x_lab, bf16, h, L.rows_pad, h, 64)) return rc;
+  // Tensor maps (tile offsets are TMA coordinates). The three G buffers are one
+  // [NUM_GBUF * rows_pad, v_chunk] tensor; buffer b starts at row b * rows_pad.
+  CUtensorMap maps[6];  // x K-major, x MN-major, W K-major, W MN-major, G K-major, G MN-major
+  const int g_rows = NUM_GBUF * L.rows_pad;
+  if (int rc = make_map(&maps[0], x_lab, bf16, h, L.rows_pad, h, BM)) return rc;
+  if (int rc = make_map(&maps[1], x_lab, bf16, h, L.rows_pad, h, 64)) return rc;
+  if (int rc = make_map(&maps[2], weight, bf16, h, vl, h, kBN)) return rc;
+  if (int rc = make_map(&maps[3], weight, bf16, h, vl, h, 64)) return rc;
+  if (int rc = make_map(&maps[4], g, bf16, L.v_chunk, g_rows, L.v_chunk, BM)) return rc;
+  if (int rc = make_map(&maps[5], g, bf16, L.v_chunk, g_rows, L.v_chunk, 64)) return rc;
 
-  EngineParams base{};
-  base.err = d->err_ptr;
-  base.timeout_ns = wait_timeout_ns();
-  base.grad_loss = grad_loss;
-  base.denom = denom;
-  base.gscale = 32768.0f;
+  int* sync = reinterpret_cast<int*>(ws + L.sync);
+  LMCE_CUDA(cudaMemsetAsync(sync, 0, sizeof(int) * L.sync_ints, st));
 
-  const int n_chunks = (vl + L.v_chunk - 1) / L.v_chunk;
+  BwdParams p{};
+  p.rows_pad = L.rows_pad;
+  p.H = h;
+  p.V = vl;
+  p.v_chunk = L.v_chunk;
+  p.n_chunks = L.n_chunks;
+  p.count = count;
+  p.lbl_lab = lbl_lab;
+  p.lse_lab = lse_lab;
+  p.g = g;
+  p.dx_acc = dx_acc;
+  p.row_idx = row_idx;
+  p.dx_out = d_hidden;
+  p.dx_out_f32 = d_hidden_f32;
+  p.dw_out = d_weight;
+  p.want_dx = want_dx ? 1 : 0;
+  p.want_dw = want_dw ? 1 : 0;
+  p.grad_loss = grad_loss;
+  p.denom = denom;
+  p.gscale = 32768.0f;
+  p.sync = sync;
+  p.err = d->err_ptr;
+  p.timeout_ns = wait_timeout_ns();
   const int grid = d->sms;
-  for (int c = 0; c < n_chunks; ++c) {
-    const int start = c * L.v_chunk;
-    const int width = (vl - start) < L.v_chunk ? (vl - start) : L.v_chunk;
-
-    EngineParams pg = base;  // G = (softmax - onehot) * 2^15
-    pg.M = L.rows_pad;
-    pg.count_dev = count;
-    pg.N = width;
-    pg.K = h;
-    pg.b_off = start;
-    pg.v_limit = width;
-    pg.lbl_lab = lbl_lab;
-    pg.lse_lab = lse_lab;
-    pg.out = g;
-    pg.ldo = L.v_chunk;
-    if (int rc = launch_engine_dt<KIND_GRAD, false, false>(bf16, m_xlab_k, m_w_k, pg, grid, st)) return rc;
-
-    if (want_dx) {
-      EngineParams px = base;  // dX += G . W_chunk
-      px.M = L.rows_pad;
-      px.count_dev = count;
-      px.N = h;
-      px.K = width;
-      px.b_off = start;
-      px.out = d_hidden;
-      px.out_f32 = d_hidden_f32;
-      px.acc_f32 = dx_acc;
-      px.row_idx = row_idx;
-      px.ldo = h;
-      px.first = c == 0;
-      px.last = c == n_chunks - 1;
-      if (int rc = launch_engine_dt<KIND_DX, false, true>(bf16, m_g_k, m_w_mn, px, grid, st)) return rc;
-    }
-    if (want_dw) {
-      EngineParams pw = base;  // dW_chunk = G^T . X_lab
-      pw.M = width;
-      pw.count_dev = count;
-      pw.N = h;
-      pw.K = L.rows_pad;
-      pw.b_off = start;
-      pw.v_limit = width;
-      pw.out = d_weight;
-      pw.ldo = h;
-      if (int rc = launch_engine_dt<KIND_DW, true, true>(bf16, m_g_mn, m_xlab_mn, pw, grid, st)) return rc;
-    }
-  }
-  return LMCE_OK;
+  return bf16 ? launch_bwd<true>(maps, p, grid, st) : launch_bwd<false>(maps, p, grid, st);
 }
 
 int lmce_dx_finalize(const float* d_hidden_f32, int64_t n_tokens, int64_t hidden_dim, int dtype, void* d_hidden,
@@ -711,6 +716,25 @@ int lmce_selftest_wait_timeout(uint64_t timeout_ns, void* stream) {
 }
 
 uint64_t lmce_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int lmce_set_timing_events(int which, void* begin, void* end) {
+  if (which < 0 || which > 1) return fail(LMCE_ERR_INVALID_ARGUMENT, "timing slot %d", which);
+  if ((begin == nullptr) != (end == nullptr)) return fail(LMCE_ERR_INVALID_ARGUMENT, "set both events or neither");
+  if (begin != nullptr && g_event_record == nullptr) {
+    static std::once_flag once;
+    std::call_once(once, [] {
+      cudaDriverEntryPointQueryResult q;
+      void* fn = nullptr;
+      if (cudaGetDriverEntryPoint("cuEventRecord", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+          q == cudaDriverEntryPointSuccess)
+        g_event_record = reinterpret_cast<PFN_cuEventRecord_v2000>(fn);
+    });
+    if (g_event_record == nullptr) return fail(LMCE_ERR_CUDA, "cuEventRecord unavailable");
+  }
+  g_timing[which][0].store(static_cast<CUevent>(begin), std::memory_order_release);
+  g_timing[which][1].store(static_cast<CUevent>(end), std::memory_order_release);
+  return LMCE_OK;
+}
 
 }  // extern "C"
 

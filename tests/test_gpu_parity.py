@@ -185,3 +185,37 @@ def test_timeout_path_reports_error(cuda_device):
     torch.cuda.synchronize()
     assert _lib.device_error(reset=True) == _lib.LMCE_ERR_TIMEOUT
     assert _lib.device_error(reset=True) == 0
+
+
+def test_packed_batch_with_proxy(cuda_device):
+    """Padding -> pack -> head -> scatter -> proxy (ops.py:1107-1184) against eager logits."""
+    from rus_b200.packing import lm_head_with_proxy, shift_and_pack
+
+    g = torch.Generator().manual_seed(17)
+    B, S, H, V = 3, 40, 256, 5000
+    hidden = torch.randn(B, S, H, generator=g).half()
+    weight = (torch.randn(V, H, generator=g) * 0.05).half()
+    labels = torch.randint(0, V, (B, S), generator=g)
+    mask = torch.ones(B, S, dtype=torch.long)
+    mask[0, 30:] = 0
+    labels[0, 30:] = -100
+    labels[1, :10] = -100
+    packed = shift_and_pack(labels.to(cuda_device), mask.to(cuda_device))
+    hp = hidden.reshape(-1, H).to(cuda_device).index_select(0, packed.valid_idx)
+    loss, proxy = lm_head_with_proxy(hp, packed, weight.to(cuda_device))
+    z = F.linear(hidden, weight).float()
+    ref_loss = F.cross_entropy(z[:, :-1].reshape(-1, V), labels[:, 1:].reshape(-1), ignore_index=-100)
+    assert abs(loss.item() - ref_loss.item()) <= 1e-3 * abs(ref_loss.item())
+    assert proxy.shape == (B, S, V)
+    kept = torch.zeros(B * S, dtype=torch.bool)
+    kept[packed.valid_idx.cpu()] = True
+    kept = kept.view(B, S)
+    ent_ref = torch.logsumexp(z, -1) - torch.sum(F.softmax(z, -1) * z, -1)
+    ent = (torch.logsumexp(proxy, -1) - torch.sum(F.softmax(proxy, -1) * proxy, -1)).cpu()
+    assert ((ent[kept] - ent_ref[kept]).abs() <= 1e-3 * ent_ref[kept].abs().clamp(min=1)).all()
+    ok = orc.argmax_mismatch_ok(proxy.argmax(-1).cpu()[kept], z.argmax(-1)[kept], z[kept], torch.float16)
+    assert bool(ok.all())
+    for row in range(B):
+        r_ref = F.cross_entropy(z[row, :-1], labels[row, 1:], ignore_index=-100)
+        r = F.cross_entropy(proxy[row, :-1].float(), labels[row, 1:].to(cuda_device), ignore_index=-100)
+        assert abs(r.item() - r_ref.item()) <= 1e-3 * abs(r_ref.item())
