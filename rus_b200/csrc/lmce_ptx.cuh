@@ -1,5 +1,5 @@
 // Thin inline-PTX wrappers for the sm_100a features the lm_head CE kernels use:
-// mbarriers, TMA tiled loads (no cluster multicast anywhere in this library),
+// mbarriers, TMA tiled loads (every load reads this GPU's own memory into this CTA),
 // tcgen05 (TMEM alloc, UMMA issue/commit, TMEM loads) and a few scalar helpers.
 //
 // Every wait in this library is bounded: a wait that exceeds its limit returns
