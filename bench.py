@@ -359,8 +359,11 @@ def main():
     # ---- roofline of the dominant kernel (largest share of the step)
     peaks, peak_kind = load_peaks()
     v_local = v_hi - v_lo
-    k_peak = float(peaks["bf16_tflops"])
-    sust = float(peaks.get("bf16_tflops_sustained", k_peak))
+    burst = float(peaks["bf16_tflops"])
+    # Both kernels run inside a multi-millisecond step, back to back for the whole timed
+    # region, where the 1 kW power cap sets the clock: the sustained figure is the ceiling.
+    k_peak = float(peaks.get("bf16_tflops_sustained", burst))
+    sust = k_peak
     kernels = {
         "stats": {"name": "lmce_stats_kernel (fused logits GEMM + online softmax statistics)",
                   "ms": kern_ms[0], "alg_flops": 2.0 * n_tokens * H * v_local,
@@ -417,6 +420,7 @@ def main():
                 "l2": "256 MiB flush written between timed steps; W (467 MB) exceeds L2 as well",
             },
             "pct_tcgen05_peak": 100.0 * step_tflops / k_peak,
+            "pct_tcgen05_burst_peak": 100.0 * step_tflops / burst,
             "step_tflops": step_tflops,
             "peak_activation_mib": peak_act_mib,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "ms_per_step": e2e_ms_step,
@@ -428,7 +432,7 @@ def main():
                 "kernel": dom["name"],
                 "achieved": dom["achieved_tflops"], "peak": k_peak, "unit": "TFLOP/s",
                 "frac": dom["achieved_tflops"] / k_peak,
-                "peak_kind": f"{peak_kind} burst bf16 (MEASURED_PEAKS.json)",
+                "peak_kind": f"{peak_kind} sustained bf16 (MEASURED_PEAKS.json); burst {burst}",
                 "traffic": dom["traffic"] if (args.config == "c2" and world == 1) else None,
                 "launch_ms": dom["ms"], "flops_per_launch": dom["alg_flops"],
                 "executed_tflops": dom["executed_tflops"],

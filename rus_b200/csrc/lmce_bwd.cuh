@@ -192,15 +192,43 @@ __device__ __forceinline__ void publish_add(int* ctr, int v) {
   }
 }
 
+// UMMA k-loop of one tile. The operand majors and the instruction descriptor are
+// template constants: tcgen05.mma takes them from uniform registers, and values
+// that depend on the tile kind read from shared memory are not provably uniform
+// (the compiler then serialises every issue, halving the tensor-pipe rate).
+template <bool BF16, bool A_MN, bool B_MN, int STAGES>
+__device__ __forceinline__ bool mma_tile(uint8_t* smem, uint64_t* full_bar, uint64_t* empty_bar, int nkb,
+                                         uint32_t d_tmem, int& stage, uint32_t& phase, volatile int* abort_flag,
+                                         uint64_t tlimit) {
+  using C = TileCfg<false>;
+  constexpr uint32_t idesc = make_idesc_f16(BF16, A_MN, B_MN, BM, BN);
+  for (int kb = 0; kb < nkb; ++kb) {
+    if (!mbar_wait(&full_bar[stage], phase, abort_flag, tlimit)) return false;
+    tc_fence_after();
+    const uint32_t sa = smem_u32(smem + stage * C::STAGE_BYTES);
+#pragma unroll
+    for (int k = 0; k < BK / UMMA_K; ++k)
+      umma_f16_ss(d_tmem, operand_desc(sa, A_MN, k), operand_desc(sa + C::A_BYTES, B_MN, k), idesc,
+                  (kb | k) != 0 ? 1u : 0u);
+    umma_commit(&empty_bar[stage]);
+    if (++stage == STAGES) {
+      stage = 0;
+      phase ^= 1u;
+    }
+  }
+  return true;
+}
+
 template <bool BF16, int STAGES>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     lmce_bwd_kernel(const __grid_constant__ CUtensorMap map_xk, const __grid_constant__ CUtensorMap map_xmn,
                     const __grid_constant__ CUtensorMap map_wk, const __grid_constant__ CUtensorMap map_wmn,
                     const __grid_constant__ CUtensorMap map_gk, const __grid_constant__ CUtensorMap map_gmn,
                     const BwdParams p) {
+  using C = TileCfg<false>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* tfull_bar = empty_bar + STAGES;
   uint64_t* tempty_bar = tfull_bar + 2;
@@ -263,6 +291,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       bool ok = true;
       TileCursor cur;
       cur.init();
+      int g_ready_chunk = -1;    // highest chunk whose G tiles this producer saw complete
+      int gbuf_free_chunk = -1;  // highest chunk whose G buffer this producer saw released
       int next_ticket = atomicAdd(ticket, 1);  // claimed one tile ahead of its loads
       for (;;) {
         if (!mbar_wait(&sched_empty[slot], sphase ^ 1u, abort_flag, tlimit)) {
@@ -287,18 +317,28 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (!has) break;
         next_ticket = atomicAdd(ticket, 1);  // result is first needed after this tile's loads
 
-        // dependencies of this tile
+        // Dependencies of this tile. Tiles of one chunk are contiguous in the list, so a
+        // dependency seen satisfied once is remembered and later tiles skip the acquire.
         const int gbuf = t.chunk % NUM_GBUF;
         if (t.kind == BK_G) {
-          if (t.chunk >= NUM_GBUF) {
+          if (t.chunk >= NUM_GBUF && t.chunk > gbuf_free_chunk) {
             const int prev = t.chunk - NUM_GBUF;
             ok = wait_counter(&consumed[prev], geo.nDX() + geo.nDW(prev), abort_flag, tlimit);
+            if (ok) gbuf_free_chunk = t.chunk;
           }
         } else {
-          ok = wait_counter(&gdone[t.chunk], geo.nG(t.chunk), abort_flag, tlimit);
-          if (ok && t.kind == BK_DX && t.chunk > 0)
+          bool acquired = false;
+          if (t.chunk > g_ready_chunk) {
+            ok = wait_counter(&gdone[t.chunk], geo.nG(t.chunk), abort_flag, tlimit);
+            if (ok) g_ready_chunk = t.chunk;
+            acquired = true;
+          }
+          if (ok && t.kind == BK_DX && t.chunk > 0) {
             ok = wait_counter(&dxchain[t.m * geo.num_hn + t.n], t.chunk, abort_flag, tlimit);
-          asm volatile("fence.proxy.async.global;" ::: "memory");  // G was written by generic stores
+            acquired = true;
+          }
+          // G and dX were written by generic stores of other CTAs; order them before the async-proxy reads
+          if (acquired) asm volatile("fence.proxy.async.global;" ::: "memory");
         }
         if (!ok) break;
 
@@ -308,10 +348,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             ok = false;
             break;
           }
-          uint8_t* sa = smem + stage * STAGE_BYTES;
-          uint8_t* sb = sa + A_BYTES;
+          uint8_t* sa = smem + stage * C::STAGE_BYTES;
+          uint8_t* sb = sa + C::A_BYTES;
           uint64_t* fb = &full_bar[stage];
-          mbar_arrive_expect_tx(fb, STAGE_BYTES);
+          mbar_arrive_expect_tx(fb, C::STAGE_BYTES);
           const int k0 = kb * BK;
           if (t.kind == BK_G) {
             load_operand<BM>(sa, &map_xk, fb, false, t.m * BM, k0);
@@ -365,9 +405,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           sphase ^= 1u;
         }
         if (t.kind == BK_END) break;
-        const bool a_mn = t.kind == BK_DW;
-        const bool b_mn = t.kind != BK_G;
-        const uint32_t idesc = make_idesc_f16(BF16, a_mn, b_mn, BM, BN);
         if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, abort_flag, tlimit)) {
           ok = false;
           break;
@@ -375,23 +412,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
         const int nkb = geo.num_kb(t, p.H);
-        for (int kb = 0; kb < nkb; ++kb) {
-          if (!mbar_wait(&full_bar[stage], phase, abort_flag, tlimit)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
-#pragma unroll
-          for (int k = 0; k < BK / UMMA_K; ++k)
-            umma_f16_ss(d_tmem, operand_desc(sa, a_mn, k), operand_desc(sa + A_BYTES, b_mn, k), idesc,
-                        (kb | k) != 0 ? 1u : 0u);
-          umma_commit(&empty_bar[stage]);
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1u;
-          }
-        }
+        if (t.kind == BK_G)
+          ok = mma_tile<BF16, false, false, STAGES>(smem, full_bar, empty_bar, nkb, d_tmem, stage, phase, abort_flag,
+                                                     tlimit);
+        else if (t.kind == BK_DX)
+          ok = mma_tile<BF16, false, true, STAGES>(smem, full_bar, empty_bar, nkb, d_tmem, stage, phase, abort_flag,
+                                                    tlimit);
+        else
+          ok = mma_tile<BF16, true, true, STAGES>(smem, full_bar, empty_bar, nkb, d_tmem, stage, phase, abort_flag,
+                                                   tlimit);
         if (!ok) break;
         umma_commit(&tfull_bar[acc]);  // also fires when nkb == 0 (no UMMA issued)
         if (++acc == 2) {

@@ -12,6 +12,7 @@
 #include <cstring>
 #include <atomic>
 #include <mutex>
+#include <utility>
 
 #include "../../include/lmce.h"
 #include "lmce_bwd.cuh"
@@ -159,23 +160,85 @@ int ensure_smem_attr(K kern, int smem, bool* done) {
   return LMCE_OK;
 }
 
-template <bool BF16>
+// Launch with an optional cluster of 2 CTAs (pair kernels).
+template <typename... KArgs, typename... Args>
+int launch_ex(void (*kern)(KArgs...), int grid, int smem, int cluster, cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+  if (e != cudaSuccess) return fail(LMCE_ERR_CUDA, "kernel launch failed: %s", cudaGetErrorString(e));
+  return launched();
+}
+
+// Co-resident clusters of the pair kernel `kern` on the current device (cached per device and kernel).
+template <typename K>
+int max_pairs(K kern, int smem, int sms, int* cache) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return sms / 2;
+  if (cache[dev] > 0) return cache[dev];
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(sms, 1, 1);
+  cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) n = sms / 2;
+  cache[dev] = n;
+  return n;
+}
+
+template <bool BF16, bool PAIR>
 int launch_stats(const CUtensorMap& mx, const CUtensorMap& mw, const StatsParams& p, int grid, cudaStream_t st) {
-  auto kern = lmce_stats_kernel<BF16, kStages>;
-  constexpr int smem = engine_smem_bytes<kStages>();
+  auto kern = lmce_stats_kernel<BF16, PAIR>;
+  constexpr int smem = TileCfg<PAIR>::SMEM_BYTES;
   static bool done[kMaxDevices] = {};
   if (int rc = ensure_smem_attr(kern, smem, done)) return rc;
   timing_mark(0, 0, st);
-  kern<<<grid, NUM_THREADS, smem, st>>>(mx, mw, p);
-  const int rc = launched();
+  const int rc = launch_ex(kern, grid, smem, PAIR ? 2 : 1, st, mx, mw, p);
   timing_mark(0, 1, st);
   return rc;
+}
+
+// Pair kernels are used when a 256-row tile wastes no more rows than a 128-row one.
+// LMCE_TILE_MODE (compile time): 0 = that rule, 1 = always single CTA, 2 = pairs where possible.
+#ifndef LMCE_TILE_MODE
+#define LMCE_TILE_MODE 0
+#endif
+bool use_pair_tiles(int64_t rows) {
+  if (LMCE_TILE_MODE == 1) return false;
+  if (LMCE_TILE_MODE == 2) return rows > BM;
+  return rows > BM && ((rows + 255) / 256) * 256 <= ((rows + 127) / 128) * 128;
+}
+
+// Units that can run at once for the statistics kernel (CTAs, or pairs of CTAs).
+int stats_slots(bool pair, int sms) {
+  if (!pair) return sms;
+  static int cache_f16[kMaxDevices] = {}, cache_bf16[kMaxDevices] = {};
+  const int a = max_pairs(lmce_stats_kernel<false, true>, TileCfg<true>::SMEM_BYTES, sms, cache_f16);
+  const int b = max_pairs(lmce_stats_kernel<true, true>, TileCfg<true>::SMEM_BYTES, sms, cache_bf16);
+  return a < b ? a : b;
 }
 
 template <bool BF16>
 int launch_bwd(const CUtensorMap* maps, const BwdParams& p, int grid, cudaStream_t st) {
   auto kern = lmce_bwd_kernel<BF16, kStages>;
-  constexpr int smem = engine_smem_bytes<kStages>();
+  constexpr int smem = TileCfg<false>::SMEM_BYTES;
   static bool done[kMaxDevices] = {};
   if (int rc = ensure_smem_attr(kern, smem, done)) return rc;
   timing_mark(1, 0, st);
@@ -513,9 +576,11 @@ int64_t lmce_fwd_num_parts(int64_t n_tokens, int64_t vocab_local) {
   int sms = 148;
   if (device_info(&d) == LMCE_OK) sms = d->sms;
   if (n_tokens <= 0 || vocab_local <= 0) return 1;
-  const int num_m = static_cast<int>((n_tokens + BM - 1) / BM);
+  const bool pair = use_pair_tiles(n_tokens);
+  const int tile_m = pair ? 2 * BM : BM;
+  const int num_m = static_cast<int>((n_tokens + tile_m - 1) / tile_m);
   const int num_n = static_cast<int>((vocab_local + kBN - 1) / kBN);
-  return choose_slabs(num_m, num_n, sms);
+  return choose_slabs(num_m, num_n, d ? stats_slots(pair, sms) : sms);
 }
 
 int lmce_fwd_stats(const void* hidden, const void* weight, const int64_t* labels, int64_t n_tokens,
@@ -530,13 +595,15 @@ int lmce_fwd_stats(const void* hidden, const void* weight, const int64_t* labels
   DevInfo* d = nullptr;
   if (int rc = device_info(&d)) return rc;
   if (int rc = get_encoder()) return rc;
-  const int num_m = static_cast<int>((n_tokens + BM - 1) / BM);
+  const bool pair = use_pair_tiles(n_tokens);
+  const int tile_m = pair ? 2 * BM : BM;
+  const int num_m = static_cast<int>((n_tokens + tile_m - 1) / tile_m);
   const int num_n = static_cast<int>((vocab_local + kBN - 1) / kBN);
   if (n_parts < 1 || n_parts > num_n) return fail(LMCE_ERR_INVALID_ARGUMENT, "n_parts %lld out of range", (long long)n_parts);
   const bool bf16 = dtype == LMCE_DTYPE_BF16;
   CUtensorMap mx, mw;
   if (int rc = make_map(&mx, hidden, bf16, hidden_dim, n_tokens, hidden_dim, BM)) return rc;
-  if (int rc = make_map(&mw, weight, bf16, hidden_dim, vocab_local, hidden_dim, kBN)) return rc;
+  if (int rc = make_map(&mw, weight, bf16, hidden_dim, vocab_local, hidden_dim, pair ? kBN / 2 : kBN)) return rc;
   StatsParams p{};
   p.M = static_cast<int>(n_tokens);
   p.N = static_cast<int>(vocab_local);
@@ -548,9 +615,12 @@ int lmce_fwd_stats(const void* hidden, const void* weight, const int64_t* labels
   p.err = d->err_ptr;
   p.timeout_ns = wait_timeout_ns();
   const long long units = static_cast<long long>(num_m) * n_parts;
-  const int grid = static_cast<int>(units < d->sms ? units : d->sms);
+  const int slots = stats_slots(pair, d->sms);
+  const int grid = static_cast<int>(units < slots ? units : slots) * (pair ? 2 : 1);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  return bf16 ? launch_stats<true>(mx, mw, p, grid, st) : launch_stats<false>(mx, mw, p, grid, st);
+  if (pair)
+    return bf16 ? launch_stats<true, true>(mx, mw, p, grid, st) : launch_stats<false, true>(mx, mw, p, grid, st);
+  return bf16 ? launch_stats<true, false>(mx, mw, p, grid, st) : launch_stats<false, false>(mx, mw, p, grid, st);
 }
 
 int lmce_stats_reduce(const lmce_part* parts, int64_t n_parts, int64_t tok_stride, int64_t part_stride,

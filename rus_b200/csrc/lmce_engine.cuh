@@ -31,15 +31,23 @@ constexpr float LOG2E = 1.4426950408889634f;
 constexpr float LN2 = 0.6931471805599453f;
 constexpr float NEG_BIG = -1.0e30f;  // finite "minus infinity" for running maxima
 
-constexpr int A_BYTES = BM * BK * 2;          // 16 KB
-constexpr int B_BYTES = BN * BK * 2;          // 32 KB
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int MN_BOX_BYTES = 64 * BK * 2;     // one {64 MN, 64 K} TMA box of an MN-major operand
 
-template <int STAGES>
-constexpr int engine_smem_bytes() {
-  return STAGES * STAGE_BYTES + 1024 /*align slack*/ + 1024 /*barriers, schedule ring*/;
-}
+// Tile geometry. Single CTA: a 128 x 256 output tile, the CTA holds 128 A rows and
+// 256 B rows per k-block (48 KB stages, 4 of them). Pair (cta_group::2): a 256 x 256
+// output tile over two CTAs; each CTA holds 128 A rows and 128 B rows per k-block
+// (32 KB stages, 6 of them) and 128 accumulator lanes; the leader issues the UMMAs.
+template <bool PAIR>
+struct TileCfg {
+  static constexpr int TILE_M = PAIR ? 2 * BM : BM;     // output rows per tile
+  static constexpr int B_ROWS = PAIR ? BN / 2 : BN;     // B rows staged by one CTA
+  static constexpr int A_BYTES = BM * BK * 2;           // 16 KB
+  static constexpr int B_BYTES = B_ROWS * BK * 2;       // 16 or 32 KB
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = PAIR ? 6 : 4;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align slack*/ + 1024 /*barriers, ring*/;
+  static constexpr int CTAS = PAIR ? 2 : 1;
+};
 
 enum : int {
   ERR_OK = 0,
@@ -148,8 +156,8 @@ __device__ __forceinline__ uint64_t operand_desc(uint32_t base, bool mn_major, i
 // statistics each epilogue thread carries in registers.
 struct StatsSchedule {
   int num_m, num_n, n_slabs, total, num_kb;
-  __device__ __forceinline__ void init(const StatsParams& p) {
-    num_m = (p.M + BM - 1) / BM;
+  __device__ __forceinline__ void init(const StatsParams& p, int tile_m) {
+    num_m = (p.M + tile_m - 1) / tile_m;
     num_n = (p.N + BN - 1) / BN;
     num_kb = (p.K + BK - 1) / BK;
     n_slabs = p.n_slabs;
@@ -163,13 +171,15 @@ struct StatsSchedule {
   }
 };
 
-template <bool BF16, int STAGES>
+template <bool BF16, bool PAIR>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     lmce_stats_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
                       const StatsParams p) {
+  using C = TileCfg<PAIR>;
+  constexpr int STAGES = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* tfull_bar = empty_bar + STAGES;
   uint64_t* tempty_bar = tfull_bar + 2;
@@ -179,10 +189,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   const int warp = __shfl_sync(0xffffffffu, threadIdx.x / 32, 0);
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = PAIR ? cluster_rank() : 0u;          // 0 = leader (issues the UMMAs)
+  const int unit0 = PAIR ? static_cast<int>(cluster_id_x()) : static_cast<int>(blockIdx.x);
+  const int unit_step = PAIR ? static_cast<int>(cluster_count_x()) : static_cast<int>(gridDim.x);
 
   StatsSchedule sch;
-  sch.init(p);
-  if (static_cast<int>(blockIdx.x) >= sch.total) return;  // uniform for the whole CTA
+  sch.init(p, C::TILE_M);
+  if (unit0 >= sch.total) return;  // uniform for the CTA (and for both CTAs of a pair)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -191,7 +204,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull_bar[b], 1);
-      mbar_init(&tempty_bar[b], EPI_THREADS);
+      mbar_init(&tempty_bar[b], C::CTAS * EPI_THREADS);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -202,11 +215,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     tma_prefetch_desc(&map_w);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_holder, TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_holder, TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_holder, TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // peer barriers initialised before any remote arrive / copy
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
   const uint64_t tlimit = p.timeout_ns;
@@ -218,7 +237,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t phase = 0;
       int issued = 0;
       bool ok = true;
-      for (int u = blockIdx.x; ok && u < sch.total; u += gridDim.x) {
+      for (int u = unit0; ok && u < sch.total; u += unit_step) {
         int m_blk, n0, n1, slab;
         sch.unit(u, m_blk, n0, n1, slab);
         for (int n_blk = n0; ok && n_blk < n1; ++n_blk) {
@@ -227,10 +246,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               ok = false;
               break;
             }
-            uint8_t* sa = smem + stage * STAGE_BYTES;
-            mbar_arrive_expect_tx(&full_bar[stage], STAGE_BYTES);
-            load_operand<BM>(sa, &map_x, &full_bar[stage], false, m_blk * BM, kb * BK);
-            load_operand<BN>(sa + A_BYTES, &map_w, &full_bar[stage], false, n_blk * BN, kb * BK);
+            uint8_t* sa = smem + stage * C::STAGE_BYTES;
+            uint8_t* sb = sa + C::A_BYTES;
+            const int k0 = kb * BK;
+            if constexpr (PAIR) {
+              // both CTAs' copies count on the leader's full barrier
+              if (rank == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * C::STAGE_BYTES);
+              const uint32_t fb = mapa_shared(smem_u32(&full_bar[stage]), 0);
+              tma_load_2d_pair(sa, &map_x, fb, k0, m_blk * C::TILE_M + BM * static_cast<int>(rank));
+              tma_load_2d_pair(sb, &map_w, fb, k0, n_blk * BN + C::B_ROWS * static_cast<int>(rank));
+            } else {
+              mbar_arrive_expect_tx(&full_bar[stage], C::STAGE_BYTES);
+              load_operand<BM>(sa, &map_x, &full_bar[stage], false, m_blk * BM, k0);
+              load_operand<BN>(sb, &map_w, &full_bar[stage], false, n_blk * BN, k0);
+            }
             ++issued;
             if (++stage == STAGES) {
               stage = 0;
@@ -242,30 +271,34 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (!ok) {
         raise_error(p.err, ERR_TIMEOUT);
         *abort_flag = 1;
-        // Drain: wait (bounded) for the copies this thread issued into each stage.
-        const int outstanding = issued < STAGES ? issued : STAGES;
-        for (int i = 1; i <= outstanding; ++i) {
-          int s = stage - i;
-          uint32_t ph = phase;
-          if (s < 0) {
-            s += STAGES;
-            ph ^= 1u;
+        if (!PAIR || rank == 0) {
+          // Drain: wait (bounded) for the copies counted on this CTA's barriers.
+          const int outstanding = issued < STAGES ? issued : STAGES;
+          for (int i = 1; i <= outstanding; ++i) {
+            int s = stage - i;
+            uint32_t ph = phase;
+            if (s < 0) {
+              s += STAGES;
+              ph ^= 1u;
+            }
+            volatile int no_abort = 0;
+            mbar_wait(&full_bar[s], ph, &no_abort, tlimit);
           }
-          volatile int no_abort = 0;
-          mbar_wait(&full_bar[s], ph, &no_abort, tlimit);
         }
       }
     }
   } else if (warp == 1) {
     // -------------------------------------------------------- UMMA issuer ---
-    if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc_f16(BF16, false, false, BM, BN);
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = make_idesc_f16(BF16, false, false, C::TILE_M, BN);
+      const uint32_t peer_empty = PAIR ? mapa_shared(smem_u32(empty_bar), 1) : 0u;
+      const uint32_t peer_tfull = PAIR ? mapa_shared(smem_u32(tfull_bar), 1) : 0u;
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int u = blockIdx.x; ok && u < sch.total; u += gridDim.x) {
+      for (int u = unit0; ok && u < sch.total; u += unit_step) {
         int m_blk, n0, n1, slab;
         sch.unit(u, m_blk, n0, n1, slab);
         for (int n_blk = n0; ok && n_blk < n1; ++n_blk) {
@@ -281,19 +314,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               break;
             }
             tc_fence_after();
-            const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
+            const uint32_t sa = smem_u32(smem + stage * C::STAGE_BYTES);
 #pragma unroll
-            for (int k = 0; k < BK / UMMA_K; ++k)
-              umma_f16_ss(d_tmem, operand_desc(sa, false, k), operand_desc(sa + A_BYTES, false, k), idesc,
-                          (kb | k) != 0 ? 1u : 0u);
-            umma_commit(&empty_bar[stage]);
+            for (int k = 0; k < BK / UMMA_K; ++k) {
+              const uint64_t da = operand_desc(sa, false, k), db = operand_desc(sa + C::A_BYTES, false, k);
+              if constexpr (PAIR)
+                umma_f16_ss_pair(d_tmem, da, db, idesc, (kb | k) != 0 ? 1u : 0u);
+              else
+                umma_f16_ss(d_tmem, da, db, idesc, (kb | k) != 0 ? 1u : 0u);
+            }
+            if constexpr (PAIR) {
+              umma_commit_pair(smem_u32(&empty_bar[stage]));
+              umma_commit_pair(peer_empty + 8u * stage);
+            } else {
+              umma_commit(&empty_bar[stage]);
+            }
             if (++stage == STAGES) {
               stage = 0;
               phase ^= 1u;
             }
           }
           if (!ok) break;
-          umma_commit(&tfull_bar[acc]);
+          if constexpr (PAIR) {
+            umma_commit_pair(smem_u32(&tfull_bar[acc]));
+            umma_commit_pair(peer_tfull + 8u * acc);
+          } else {
+            umma_commit(&tfull_bar[acc]);
+          }
           if (++acc == 2) {
             acc = 0;
             acc_phase ^= 1u;
@@ -305,23 +352,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         *abort_flag = 1;
       }
       // Make sure every UMMA this thread issued has retired before TMEM is freed.
-      umma_commit(drain_bar);
+      if constexpr (PAIR)
+        umma_commit_pair(smem_u32(drain_bar));
+      else
+        umma_commit(drain_bar);
       volatile int no_abort = 0;
       mbar_wait(drain_bar, 0, &no_abort, tlimit);
     }
   } else {
     // ---------------------------------------------------------- epilogue ---
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
-    const int r_in_tile = q * 32 + lane;
+    const int r_in_tile = BM * static_cast<int>(rank) + q * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+    const uint32_t leader_tempty = PAIR ? mapa_shared(smem_u32(tempty_bar), 0) : 0u;
     int acc = 0;
     uint32_t acc_phase = 0;
     bool ok = true;
 
-    for (int u = blockIdx.x; ok && u < sch.total; u += gridDim.x) {
+    for (int u = unit0; ok && u < sch.total; u += unit_step) {
       int m_blk, n0, n1, slab;
       sch.unit(u, m_blk, n0, n1, slab);
-      const int row = m_blk * BM + r_in_tile;
+      const int row = m_blk * C::TILE_M + r_in_tile;
 
       float st_m = NEG_BIG, st_s = 0.f, st_w = 0.f, st_best = -INFINITY, st_zy = -INFINITY;
       int st_idx = 0x7fffffff;
@@ -389,7 +440,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
         }
         tc_fence_before();
-        mbar_arrive(&tempty_bar[acc]);
+        if constexpr (PAIR)
+          mbar_arrive_cluster(leader_tempty + 8u * acc);
+        else
+          mbar_arrive(&tempty_bar[acc]);
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1u;
@@ -412,10 +466,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // the leader's UMMAs into the peer's TMEM have drained
   tc_fence_after();
   if (warp == 1) {
     __syncwarp();
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    if constexpr (PAIR)
+      tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    else
+      tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
 
