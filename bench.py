@@ -237,6 +237,8 @@ def main():
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
     group = None
+    # keep stdout to the one JSON line: NCCL's version banner goes to stdout at init
+    os.environ.setdefault("NCCL_DEBUG", "WARN")
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
@@ -356,6 +358,11 @@ def main():
     h2d = Xh.numel() * Xh.element_size() + yh.numel() * yh.element_size()
 
     stage("report")
+    dx_exchange = "none (single GPU)"
+    if world > 1:
+        from rus_b200.sharded import nvls_dx_buffer
+        dx_exchange = ("in-kernel NVLink SHARP sum (multimem.red)" if nvls_dx_buffer(n_tokens, H, device, group)
+                       is not None else "NCCL all-reduce (fp32)")
     # ---- roofline of the dominant kernel (largest share of the step)
     peaks, peak_kind = load_peaks()
     v_local = v_hi - v_lo
@@ -417,6 +424,7 @@ def main():
                 "H": H, "V": V,
                 "parallelism": "single-gpu" if world == 1 else f"vocab-sharded tp{world} ({args.scaling})",
                 "v_chunk": args.v_chunk,
+                "dx_exchange": dx_exchange,
                 "l2": "256 MiB flush written between timed steps; W (467 MB) exceeds L2 as well",
             },
             "pct_tcgen05_peak": 100.0 * step_tflops / k_peak,

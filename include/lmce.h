@@ -126,6 +126,22 @@ LMCE_API int lmce_backward(const void* hidden, const void* weight, const int64_t
                   const float* grad_loss, const float* denom, void* d_hidden, float* d_hidden_f32,
                   void* d_weight, int64_t v_chunk, void* workspace, size_t workspace_bytes, void* stream);
 
+/* lmce_backward for a vocab-sharded head with the cross-GPU dX sum fused into
+ * the kernel: the dX rows of the last vocab chunk are added, as each tile
+ * finishes, into `d_hidden_multicast` with NVLink SHARP reductions
+ * (multimem.red), so the switch sums every rank's contribution into every
+ * rank's copy while the remaining tiles compute. `d_hidden_multicast` must be
+ * the multicast address of an fp32 [n_tokens, hidden_dim] buffer that every
+ * rank of the group has zeroed before any rank starts this call (barrier), and
+ * the ranks must synchronise again before reading the sum. Replaces the
+ * reference-side gap of ops.py:320-338 (single GPU there) plus a separate
+ * all-reduce. */
+LMCE_API int lmce_backward_nvls(const void* hidden, const void* weight, const int64_t* labels, const float* lse,
+                                int64_t n_tokens, int64_t hidden_dim, int64_t vocab_local, int64_t vocab_offset,
+                                int dtype, const float* grad_loss, const float* denom, float* d_hidden_multicast,
+                                void* d_weight, int64_t v_chunk, void* workspace, size_t workspace_bytes,
+                                void* stream);
+
 /* d_hidden = dtype(d_hidden_f32), elementwise over n_tokens x hidden_dim. */
 LMCE_API int lmce_dx_finalize(const float* d_hidden_f32, int64_t n_tokens, int64_t hidden_dim, int dtype,
                      void* d_hidden, void* stream);

@@ -62,6 +62,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _int,
         [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _vp, _vp, _vp, _vp, _vp, _i64, _vp, ctypes.c_size_t, _vp],
     ),
+    "lmce_backward_nvls": (
+        _int,
+        [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _vp, _vp, _vp, _vp, _i64, _vp, ctypes.c_size_t, _vp],
+    ),
     "lmce_dx_finalize": (_int, [_vp, _i64, _i64, _int, _vp, _vp]),
     "lmce_selftest_wait_timeout": (_int, [ctypes.c_uint64, _vp]),
     "lmce_launch_count": (ctypes.c_uint64, []),

@@ -53,6 +53,8 @@ struct BwdParams {
   const int* row_idx;      // compacted row -> token row
   void* dx_out;            // [N][H] input dtype (nullable)
   float* dx_out_f32;       // [N][H] fp32 (nullable; vocab-sharded runs)
+  float* dx_mc;            // multicast address of a zeroed fp32 [N][H] buffer on every rank (nullable):
+                           // the last chunk adds this rank's dX rows into it through the switch
   void* dw_out;            // [V][H] input dtype (nullable)
   int want_dx, want_dw;
   const float* grad_loss;  // device scalar (nullable: 1)
@@ -532,6 +534,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 __stcg(reinterpret_cast<float4*>(accp + j), make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
             } else {
               const size_t trow = static_cast<size_t>(p.row_idx[row]);
+              if (p.dx_mc != nullptr) {
+                float* dst = p.dx_mc + trow * p.H + col0;
+#pragma unroll
+                for (int j = 0; j < 32; j += 4) multimem_red_add_v4_f32(dst + j, v[j], v[j + 1], v[j + 2], v[j + 3]);
+              }
               if (p.dx_out_f32 != nullptr) {
                 float* dst = p.dx_out_f32 + trow * p.H + col0;
 #pragma unroll

@@ -664,10 +664,14 @@ size_t lmce_bwd_workspace_bytes(int64_t n_tokens, int64_t hidden_dim, int64_t vo
   return bwd_layout(n_tokens, hidden_dim, vocab_local, v_chunk).total;
 }
 
-int lmce_backward(const void* hidden, const void* weight, const int64_t* labels, const float* lse,
-                  int64_t n_tokens, int64_t hidden_dim, int64_t vocab_local, int64_t vocab_offset, int dtype,
-                  const float* grad_loss, const float* denom, void* d_hidden, float* d_hidden_f32,
-                  void* d_weight, int64_t v_chunk, void* workspace, size_t workspace_bytes, void* stream) {
+}  // extern "C"
+
+namespace {
+
+int backward_impl(const void* hidden, const void* weight, const int64_t* labels, const float* lse, int64_t n_tokens,
+                  int64_t hidden_dim, int64_t vocab_local, int64_t vocab_offset, int dtype, const float* grad_loss,
+                  const float* denom, void* d_hidden, float* d_hidden_f32, float* d_hidden_mc, void* d_weight,
+                  int64_t v_chunk, void* workspace, size_t workspace_bytes, void* stream) {
   if (!hidden || !weight || !labels || !lse || !denom || !workspace)
     return fail(LMCE_ERR_INVALID_ARGUMENT, "null pointer");
   if (n_tokens <= 0 || n_tokens > (1ll << 30)) return fail(LMCE_ERR_INVALID_ARGUMENT, "bad n_tokens");
@@ -676,6 +680,7 @@ int lmce_backward(const void* hidden, const void* weight, const int64_t* labels,
   if (hidden_dim <= 0 || hidden_dim % 64 != 0) return fail(LMCE_ERR_UNSUPPORTED, "hidden_dim must be a positive multiple of 64");
   if (dtype != LMCE_DTYPE_F16 && dtype != LMCE_DTYPE_BF16) return fail(LMCE_ERR_UNSUPPORTED, "dtype %d", dtype);
   if ((d_hidden && !aligned16(d_hidden)) || (d_hidden_f32 && !aligned16(d_hidden_f32)) ||
+      (d_hidden_mc && !aligned16(d_hidden_mc)) ||
       (d_weight && !aligned16(d_weight)) || !aligned16(workspace))
     return fail(LMCE_ERR_INVALID_ARGUMENT, "output/workspace buffers must be 16-byte aligned");
   const BwdLayout L = bwd_layout(n_tokens, hidden_dim, vocab_local, v_chunk);
@@ -710,7 +715,7 @@ int lmce_backward(const void* hidden, const void* weight, const int64_t* labels,
     if (int rc = launched()) return rc;
   }
 
-  const bool want_dx = d_hidden != nullptr || d_hidden_f32 != nullptr;
+  const bool want_dx = d_hidden != nullptr || d_hidden_f32 != nullptr || d_hidden_mc != nullptr;
   const bool want_dw = d_weight != nullptr;
   if (!want_dx && !want_dw) return LMCE_OK;
 
@@ -742,6 +747,7 @@ int lmce_backward(const void* hidden, const void* weight, const int64_t* labels,
   p.row_idx = row_idx;
   p.dx_out = d_hidden;
   p.dx_out_f32 = d_hidden_f32;
+  p.dx_mc = d_hidden_mc;
   p.dw_out = d_weight;
   p.want_dx = want_dx ? 1 : 0;
   p.want_dw = want_dw ? 1 : 0;
@@ -753,6 +759,28 @@ int lmce_backward(const void* hidden, const void* weight, const int64_t* labels,
   p.timeout_ns = wait_timeout_ns();
   const int grid = d->sms;
   return bf16 ? launch_bwd<true>(maps, p, grid, st) : launch_bwd<false>(maps, p, grid, st);
+}
+
+}  // namespace
+
+extern "C" {
+
+int lmce_backward(const void* hidden, const void* weight, const int64_t* labels, const float* lse,
+                  int64_t n_tokens, int64_t hidden_dim, int64_t vocab_local, int64_t vocab_offset, int dtype,
+                  const float* grad_loss, const float* denom, void* d_hidden, float* d_hidden_f32,
+                  void* d_weight, int64_t v_chunk, void* workspace, size_t workspace_bytes, void* stream) {
+  return backward_impl(hidden, weight, labels, lse, n_tokens, hidden_dim, vocab_local, vocab_offset, dtype, grad_loss,
+                       denom, d_hidden, d_hidden_f32, nullptr, d_weight, v_chunk, workspace, workspace_bytes, stream);
+}
+
+int lmce_backward_nvls(const void* hidden, const void* weight, const int64_t* labels, const float* lse,
+                       int64_t n_tokens, int64_t hidden_dim, int64_t vocab_local, int64_t vocab_offset, int dtype,
+                       const float* grad_loss, const float* denom, float* d_hidden_multicast, void* d_weight,
+                       int64_t v_chunk, void* workspace, size_t workspace_bytes, void* stream) {
+  if (d_hidden_multicast == nullptr) return fail(LMCE_ERR_INVALID_ARGUMENT, "null multicast dX buffer");
+  return backward_impl(hidden, weight, labels, lse, n_tokens, hidden_dim, vocab_local, vocab_offset, dtype, grad_loss,
+                       denom, nullptr, nullptr, d_hidden_multicast, d_weight, v_chunk, workspace, workspace_bytes,
+                       stream);
 }
 
 int lmce_dx_finalize(const float* d_hidden_f32, int64_t n_tokens, int64_t hidden_dim, int dtype, void* d_hidden,

@@ -259,6 +259,16 @@ __device__ __forceinline__ void umma_commit_pair(uint32_t cluster_addr) {
                : "memory");
 }
 
+// --------------------------------------------------- NVLink SHARP reduction ---
+
+// out[0..3] += v on every GPU bound to the multicast address `mc` (the switch
+// reduces the contributions of all GPUs and writes the sum to each of them).
+__device__ __forceinline__ void multimem_red_add_v4_f32(float* mc, float a, float b, float c, float d) {
+  asm volatile("multimem.red.relaxed.sys.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc), "f"(a), "f"(b),
+               "f"(c), "f"(d)
+               : "memory");
+}
+
 // ------------------------------------------------------ UMMA descriptors ---
 
 // Shared-memory matrix descriptor (sm_100 format, version 1) for a 128-byte

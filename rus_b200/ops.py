@@ -177,6 +177,26 @@ def head_backward(h2d, weight, labels, lse, grad_loss, denom, want_dx: bool, wan
     return dx, dw
 
 
+def head_backward_nvls(h2d, weight, labels, lse, grad_loss, denom, dx_multicast_ptr: int, want_dw: bool,
+                       v_chunk: int = V_CHUNK_DEFAULT, vocab_offset: int = 0):
+    """Backward of one vocab shard whose dX rows are summed across the group inside the
+    kernel, into the multicast buffer at ``dx_multicast_ptr`` (lmce_backward_nvls)."""
+    n, h = h2d.shape
+    v = weight.shape[0]
+    dev = h2d.device
+    lib = _lib.load()
+    ws_bytes = int(lib.lmce_bwd_workspace_bytes(n, h, v, v_chunk))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    dw = torch.empty_like(weight) if want_dw else None
+    gl = grad_loss.detach().to(device=dev, dtype=torch.float32).reshape(1).contiguous()
+    _lib.call("lmce_backward_nvls", h2d.data_ptr(), weight.data_ptr(), labels.data_ptr(), lse.data_ptr(), n, h, v,
+              vocab_offset, _DTYPES[h2d.dtype], gl.data_ptr(), denom.data_ptr(), dx_multicast_ptr, _ptr(dw),
+              v_chunk, ws.data_ptr(), ws_bytes, _stream(dev))
+    if _debug_sync():
+        _raise_device_error()
+    return dw
+
+
 def _raise_device_error() -> None:
     code = _lib.device_error(reset=True)
     if code != _lib.LMCE_OK:

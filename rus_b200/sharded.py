@@ -8,19 +8,27 @@ hidden states and labels are replicated. The two exchange steps:
   (NCCL over NVLink, R x N x 24 bytes) and every rank merges them with
   ``lmce_stats_finish`` into identical lse / nll / entropy / argmax / loss.
 * backward: each rank contracts its shard's gradient tile into its local dW
-  shard and an fp32 dX contribution; the dX contributions are summed with one
-  all-reduce and cast to the input dtype (``lmce_dx_finalize``).
+  shard and an fp32 dX contribution, which is summed over the ranks and cast to
+  the input dtype (``lmce_dx_finalize``). When the GPUs share an NVLink switch
+  with multicast (NVLS) support, the sum is fused into the backward kernel: the
+  last vocab chunk's dX tiles are added into a symmetric multicast buffer with
+  ``multimem.red`` as they finish (``lmce_backward_nvls``), so the reduction
+  overlaps the remaining tiles and no separate all-reduce runs. Otherwise one
+  NCCL all-reduce sums the fp32 contributions.
 
 The reference has no multi-GPU path (it pins one T4); this is the B200 build's
 addition for the same operator interface.
 """
 from __future__ import annotations
 
+import os
+
 import torch
 import torch.distributed as dist
 
 from . import _lib
-from .ops import V_CHUNK_DEFAULT, _check_inputs, _stream, head_backward, head_finish, head_forward_stats
+from .ops import (V_CHUNK_DEFAULT, _check_inputs, _stream, head_backward, head_backward_nvls, head_finish,
+                  head_forward_stats)
 
 
 def shard_range(vocab_size: int, rank: int, world: int) -> tuple[int, int]:
@@ -43,6 +51,43 @@ def exchange_records(record: torch.Tensor, group=None) -> torch.Tensor:
 def reduce_dx(dx_f32: torch.Tensor, group=None) -> torch.Tensor:
     dist.all_reduce(dx_f32, op=dist.ReduceOp.SUM, group=group)
     return dx_f32
+
+
+_NVLS_CACHE: dict = {}
+
+
+def _group_name(group) -> str:
+    return (group if group is not None else dist.group.WORLD).group_name
+
+
+def nvls_dx_buffer(n: int, h: int, device: torch.device, group=None):
+    """(fp32 [n, h] symmetric tensor, handle) with a multicast mapping on every rank of
+    the group, or None when the group cannot use NVLink SHARP (the decision is made
+    jointly, so every rank takes the same path). Cached per shape. LMCE_NVLS=0 disables."""
+    if os.environ.get("LMCE_NVLS", "1") == "0" or device.type != "cuda":
+        return None
+    key = (device.index, _group_name(group), n, h)
+    if key in _NVLS_CACHE:
+        return _NVLS_CACHE[key]
+    buf = None
+    ok = 1
+    try:
+        import torch.distributed._symmetric_memory as symm_mem
+
+        t = symm_mem.empty((n, h), dtype=torch.float32, device=device)
+        hdl = symm_mem.rendezvous(t, _group_name(group))
+        if int(getattr(hdl, "multicast_ptr", 0)) == 0 or int(getattr(hdl, "offset", 0)) != 0:
+            ok = 0
+        else:
+            buf = (t, hdl)
+    except Exception:
+        ok = 0
+    flag = torch.tensor([ok], dtype=torch.int32, device=device)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
+    if int(flag.item()) == 0:
+        buf = None
+    _NVLS_CACHE[key] = buf
+    return buf
 
 
 class VocabShardedLMHeadFn(torch.autograd.Function):
@@ -76,18 +121,31 @@ class VocabShardedLMHeadFn(torch.autograd.Function):
         want_dx = ctx.needs_input_grad[0]
         want_dw = ctx.needs_input_grad[2]
         dx_f32 = None
-        with torch.cuda.device(h2d.device):
-            if want_dx:
-                dx_f32 = torch.zeros(h2d.shape, dtype=torch.float32, device=h2d.device)
-            # every rank takes the same collective steps, whatever it needs locally
-            _, dw = head_backward(h2d, w, labels, lse, grad_loss, denom, want_dx, want_dw, ctx.v_chunk,
-                                  vocab_offset=ctx.vocab_offset, dx_f32=dx_f32)
+        dev = h2d.device
+        n, h = h2d.shape
+        with torch.cuda.device(dev):
+            nvls = nvls_dx_buffer(n, h, dev, ctx.group) if want_dx else None
+            if nvls is not None:
+                # fused: the kernel adds this rank's dX rows into every rank's copy through the switch
+                dx_f32, hdl = nvls
+                dx_f32.zero_()
+                hdl.barrier(channel=0)  # every rank zeroed before any rank adds
+                dw = head_backward_nvls(h2d, w, labels, lse, grad_loss, denom, int(hdl.multicast_ptr), want_dw,
+                                        ctx.v_chunk, ctx.vocab_offset)
+                hdl.barrier(channel=0)  # every rank's additions have landed
+            else:
+                if want_dx:
+                    dx_f32 = torch.zeros(h2d.shape, dtype=torch.float32, device=dev)
+                # every rank takes the same collective steps, whatever it needs locally
+                _, dw = head_backward(h2d, w, labels, lse, grad_loss, denom, want_dx, want_dw, ctx.v_chunk,
+                                      vocab_offset=ctx.vocab_offset, dx_f32=dx_f32)
+                if want_dx:
+                    reduce_dx(dx_f32, ctx.group)
             dx = None
             if want_dx:
-                reduce_dx(dx_f32, ctx.group)
                 dx = torch.empty_like(h2d)
-                _lib.call("lmce_dx_finalize", dx_f32.data_ptr(), h2d.shape[0], h2d.shape[1],
-                          0 if h2d.dtype == torch.float16 else 1, dx.data_ptr(), _stream(h2d.device))
+                _lib.call("lmce_dx_finalize", dx_f32.data_ptr(), n, h, 0 if h2d.dtype == torch.float16 else 1,
+                          dx.data_ptr(), _stream(dev))
                 dx = dx.view(ctx.orig_shape)
         return dx, None, dw, None, None, None, None, None
 

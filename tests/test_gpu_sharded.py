@@ -42,23 +42,34 @@ def _worker(rank, world, port, q):
         y = torch.randint(0, V, (N,), generator=g)
         y[torch.rand(N, generator=g) < 0.2] = -100
         y = y.to(dev)
+        from rus_b200.sharded import nvls_dx_buffer
+
         lo, hi = shard_range(V, rank, world)
-        xs = X.clone().requires_grad_(True)
-        ws = W[lo:hi].clone().requires_grad_(True)
-        loss, nll, ent, arg = sharded_lm_head(xs, y, ws, lo, V, None, None, 4096)
-        loss.backward()
         xr = X.clone().requires_grad_(True)
         wr = W.clone().requires_grad_(True)
         loss_r, nll_r, ent_r, arg_r = chunked_lm_head(xr, y, wr, None, 4096)
         loss_r.backward()
-        torch.cuda.synchronize()
-        ok = abs(loss.item() - loss_r.item()) <= 1e-4 * abs(loss_r.item())
-        ok &= bool(((nll - nll_r).abs() <= 1e-4 * nll_r.abs().clamp(min=1)).all())
-        ok &= bool(((ent - ent_r).abs() <= 1e-4 * ent_r.abs().clamp(min=1)).all())
-        ok &= bool(torch.equal(arg, arg_r))
-        ok &= orc.rel_l2(xs.grad.float(), xr.grad.float()) < 1e-3
-        ok &= orc.rel_l2(ws.grad.float(), wr.grad[lo:hi].float()) < 1e-3
-        q.put((rank, bool(ok), ""))
+        ok = True
+        msg = ""
+        for mode in ("auto", "nccl"):  # auto: NVLink SHARP in-kernel dX sum when available
+            os.environ["LMCE_NVLS"] = "0" if mode == "nccl" else "1"
+            xs = X.clone().requires_grad_(True)
+            ws = W[lo:hi].clone().requires_grad_(True)
+            for _ in range(2):  # twice: the cached symmetric buffer is reused
+                xs.grad = None
+                ws.grad = None
+                loss, nll, ent, arg = sharded_lm_head(xs, y, ws, lo, V, None, None, 4096)
+                loss.backward()
+            torch.cuda.synchronize()
+            ok &= abs(loss.item() - loss_r.item()) <= 1e-4 * abs(loss_r.item())
+            ok &= bool(((nll - nll_r).abs() <= 1e-4 * nll_r.abs().clamp(min=1)).all())
+            ok &= bool(((ent - ent_r).abs() <= 1e-4 * ent_r.abs().clamp(min=1)).all())
+            ok &= bool(torch.equal(arg, arg_r))
+            ok &= orc.rel_l2(xs.grad.float(), xr.grad.float()) < 1e-3
+            ok &= orc.rel_l2(ws.grad.float(), wr.grad[lo:hi].float()) < 1e-3
+            if mode == "auto":
+                msg = "nvls" if nvls_dx_buffer(N, H, dev) is not None else "nccl-fallback"
+        q.put((rank, bool(ok), msg))
         dist.barrier()
         dist.destroy_process_group()
     except Exception as e:
@@ -86,3 +97,4 @@ def test_vocab_sharded_matches_single_gpu():
             p.kill()
     for rank, (ok, msg) in sorted(res.items()):
         assert ok, f"rank {rank}: {msg}"
+    print("dX exchange used:", res[0][1])
