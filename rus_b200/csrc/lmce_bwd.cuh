@@ -32,6 +32,9 @@ namespace lmce {
 
 constexpr int NUM_GBUF = 3;
 constexpr int SCHED_DEPTH = 4;
+constexpr int DX_STAGE_LD = 36;                              // floats per staged row (32 + 4 pad)
+constexpr int DX_STAGE_BYTES = BM * DX_STAGE_LD * 4;          // 18 KB
+constexpr int BWD_SMEM_BYTES = TileCfg<false>::SMEM_BYTES + DX_STAGE_BYTES;
 
 enum : int { BK_END = -1, BK_G = 0, BK_DX = 1, BK_DW = 2 };
 
@@ -240,6 +243,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   BwdTile* ring = reinterpret_cast<BwdTile*>(sched_empty + SCHED_DEPTH);
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(ring + SCHED_DEPTH);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  // epilogue staging for the coalesced cross-GPU dX reduction (after the barrier block)
+  float* dx_stage = reinterpret_cast<float*>(smem + STAGES * C::STAGE_BYTES + 1024);
 
   const int warp = __shfl_sync(0xffffffffu, threadIdx.x / 32, 0);
   const int lane = threadIdx.x & 31;
@@ -534,11 +539,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 __stcg(reinterpret_cast<float4*>(accp + j), make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
             } else {
               const size_t trow = static_cast<size_t>(p.row_idx[row]);
-              if (p.dx_mc != nullptr) {
-                float* dst = p.dx_mc + trow * p.H + col0;
-#pragma unroll
-                for (int j = 0; j < 32; j += 4) multimem_red_add_v4_f32(dst + j, v[j], v[j + 1], v[j + 2], v[j + 3]);
-              }
               if (p.dx_out_f32 != nullptr) {
                 float* dst = p.dx_out_f32 + trow * p.H + col0;
 #pragma unroll
@@ -547,6 +547,30 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               }
               if (p.dx_out != nullptr) store32_dtype<BF16>(reinterpret_cast<char*>(p.dx_out) + (trow * p.H + col0) * 2, v);
             }
+          }
+          if (p.dx_mc != nullptr && t.chunk + 1 == geo.C && col0 < p.H) {
+            // Cross-GPU sum of the finished dX rows through the switch. One thread per row would
+            // issue 32 scattered 16-byte reductions per warp instruction; staging the 128 x 32
+            // slice in shared memory lets each instruction cover 4 rows x 128 contiguous bytes.
+            float* stage_f = dx_stage + r_in_tile * DX_STAGE_LD;
+            const bool live = row < geo.n_lab;
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+              *reinterpret_cast<float4*>(stage_f + j) =
+                  live ? make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]) : make_float4(0.f, 0.f, 0.f, 0.f);
+            epilogue_bar();
+            const int wq = (warp - 2) * 32;  // 32 staged rows handled by this warp
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int r = wq + i * 4 + (lane >> 3);
+              const int grow = t.m * BM + r;
+              if (grow < geo.n_lab) {
+                const float4 f = *reinterpret_cast<const float4*>(dx_stage + r * DX_STAGE_LD + (lane & 7) * 4);
+                float* dst = p.dx_mc + static_cast<size_t>(p.row_idx[grow]) * p.H + col0 + (lane & 7) * 4;
+                multimem_red_add_v4_f32(dst, f.x, f.y, f.z, f.w);
+              }
+            }
+            epilogue_bar();
           }
         } else {  // BK_DW
           if (row < w && col0 < p.H) {

@@ -238,7 +238,7 @@ int stats_slots(bool pair, int sms) {
 template <bool BF16>
 int launch_bwd(const CUtensorMap* maps, const BwdParams& p, int grid, cudaStream_t st) {
   auto kern = lmce_bwd_kernel<BF16, kStages>;
-  constexpr int smem = TileCfg<false>::SMEM_BYTES;
+  constexpr int smem = BWD_SMEM_BYTES;
   static bool done[kMaxDevices] = {};
   if (int rc = ensure_smem_attr(kern, smem, done)) return rc;
   timing_mark(1, 0, st);

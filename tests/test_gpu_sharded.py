@@ -51,7 +51,7 @@ def _worker(rank, world, port, q):
         loss_r.backward()
         ok = True
         msg = ""
-        for mode in ("auto", "nccl"):  # auto: NVLink SHARP in-kernel dX sum when available
+        for mode in ("auto", "nccl"):  # auto: NVLink SHARP in-kernel dX sum when the switch supports it
             os.environ["LMCE_NVLS"] = "0" if mode == "nccl" else "1"
             xs = X.clone().requires_grad_(True)
             ws = W[lo:hi].clone().requires_grad_(True)
