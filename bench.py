@@ -43,9 +43,9 @@ CONFIGS = {
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM bytes (read + write) of one forward-statistics launch at config 2, from
 # one `ncu --set full` capture (profiles/lmce_head_c2_fwd_bwd.md).
-FWD_STATS_TRAFFIC_C2 = 499_676_416 + 5_951_744
-# DRAM bytes of one persistent backward launch at config 2 (same profile file); None until captured.
-BWD_TRAFFIC_C2 = None
+FWD_STATS_TRAFFIC_C2 = 504_142_000 + 5_926_000
+# DRAM bytes of one persistent backward launch at config 2 (same profile file).
+BWD_TRAFFIC_C2 = 1_827_362_000 + 1_234_519_000
 
 
 def load_peaks():
