@@ -513,9 +513,21 @@ struct BwdLayout {
   int rows_pad, v_chunk, n_chunks, sync_ints;
 };
 
+// Default vocab chunk of the backward: G buffers of about 64 MiB. Few tokens per chunk
+// leave the dX chain and the per-chunk dependencies exposed, so small N prefers wide
+// chunks; large N prefers narrower ones to keep the chunk working set near L2.
+int64_t auto_v_chunk(int64_t rows_pad) {
+  int64_t vc = (64ll << 20) / (2 * rows_pad);
+  vc = vc / 2048 * 2048;
+  if (vc < 8192) vc = 8192;
+  if (vc > 32768) vc = 32768;
+  return vc;
+}
+
 BwdLayout bwd_layout(int64_t n, int64_t h, int64_t v_local, int64_t v_chunk) {
   BwdLayout L{};
-  int64_t vc = v_chunk <= 0 ? 8192 : v_chunk;
+  const int64_t rows_pad = (n + BM - 1) / BM * BM;
+  int64_t vc = v_chunk <= 0 ? auto_v_chunk(rows_pad) : v_chunk;
   vc = (vc + 255) / 256 * 256;
   const int64_t vmax = (v_local + 255) / 256 * 256;
   if (vc > vmax) vc = vmax;

@@ -15,6 +15,7 @@ contract of fokyso82002-rgb/rus ``solution/ops.py:174-349``:
   clamped to >= 1 (ops.py:268-277). ``per_token_nll``, ``per_token_entropy``
   (fp32) and ``per_token_argmax`` (int64) are flat [N] and non-differentiable
   (ops.py:326-330).
+* ``v_chunk`` is the vocab chunk of the gradient pass (default: chosen by the library).
 * ``backward`` returns dX in the dtype and shape of ``hidden_states`` and, when
   ``weight.requires_grad``, dW in the dtype of ``weight``. (The reference
   returns ``None`` for the weight, ops.py:339; its gradient pass is also never
@@ -34,7 +35,7 @@ import torch
 
 from . import _lib
 
-V_CHUNK_DEFAULT = 8192
+V_CHUNK_DEFAULT = 8192  # the reference's default chunk; pass it explicitly to force that chunk width
 
 _DTYPES = {torch.float16: _lib.LMCE_DTYPE_F16, torch.bfloat16: _lib.LMCE_DTYPE_BF16}
 
@@ -140,12 +141,13 @@ def head_finish(parts: torch.Tensor, n_parts: int, tok_stride: int, part_stride:
 
 
 def head_backward(h2d, weight, labels, lse, grad_loss, denom, want_dx: bool, want_dw: bool,
-                  v_chunk: int = V_CHUNK_DEFAULT, vocab_offset: int = 0, dx_f32: torch.Tensor | None = None):
+                  v_chunk: int | None = None, vocab_offset: int = 0, dx_f32: torch.Tensor | None = None):
     """Recompute logits per vocab chunk and contract G into dX / dW (no [N, V] buffer)."""
     n, h = h2d.shape
     v = weight.shape[0]
     dev = h2d.device
     lib = _lib.load()
+    v_chunk = int(v_chunk or 0)
     ws_bytes = int(lib.lmce_bwd_workspace_bytes(n, h, v, v_chunk))
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
     dx = torch.empty_like(h2d) if (want_dx and dx_f32 is None) else None
@@ -178,13 +180,14 @@ def head_backward(h2d, weight, labels, lse, grad_loss, denom, want_dx: bool, wan
 
 
 def head_backward_nvls(h2d, weight, labels, lse, grad_loss, denom, dx_multicast_ptr: int, want_dw: bool,
-                       v_chunk: int = V_CHUNK_DEFAULT, vocab_offset: int = 0):
+                       v_chunk: int | None = None, vocab_offset: int = 0):
     """Backward of one vocab shard whose dX rows are summed across the group inside the
     kernel, into the multicast buffer at ``dx_multicast_ptr`` (lmce_backward_nvls)."""
     n, h = h2d.shape
     v = weight.shape[0]
     dev = h2d.device
     lib = _lib.load()
+    v_chunk = int(v_chunk or 0)
     ws_bytes = int(lib.lmce_bwd_workspace_bytes(n, h, v, v_chunk))
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
     dw = torch.empty_like(weight) if want_dw else None
@@ -208,8 +211,7 @@ class FusedChunkedLMHeadFn(torch.autograd.Function):
     ``hidden_states @ weight.T`` without materialising the [N, V] logits."""
 
     @staticmethod
-    def forward(ctx, hidden_states, shift_labels, weight_or_host_head, num_items_in_batch=None,
-                v_chunk=V_CHUNK_DEFAULT):
+    def forward(ctx, hidden_states, shift_labels, weight_or_host_head, num_items_in_batch=None, v_chunk=None):
         weight = weight_or_host_head
         _check_inputs(hidden_states, shift_labels, weight)
         h2d = hidden_states.contiguous().view(-1, hidden_states.shape[-1])
@@ -233,7 +235,7 @@ class FusedChunkedLMHeadFn(torch.autograd.Function):
                                                               num_items_in_batch)
         ctx.save_for_backward(h2d, w, labels, lse, denom)
         ctx.orig_shape = hidden_states.shape
-        ctx.v_chunk = int(v_chunk) if v_chunk else V_CHUNK_DEFAULT
+        ctx.v_chunk = int(v_chunk) if v_chunk else 0  # 0: the library's default chunk
         ctx.mark_non_differentiable(nll, ent, arg)
         return loss, nll, ent, arg
 
@@ -256,7 +258,10 @@ class FusedChunkedLMHeadFn(torch.autograd.Function):
 
 
 def chunked_lm_head(hidden_states, shift_labels, weight_or_host_head, num_items_in_batch=None,
-                    v_chunk: int = V_CHUNK_DEFAULT):
-    """Drop-in for ``solution.ops.chunked_lm_head`` (ops.py:342-349)."""
+                    v_chunk: int | None = None):
+    """Drop-in for ``solution.ops.chunked_lm_head`` (ops.py:342-349).
+
+    ``v_chunk`` is the vocab chunk of the gradient pass; ``None`` (the default) lets the
+    library size it (gradient buffers of ~64 MiB), an explicit value is used as given."""
     return FusedChunkedLMHeadFn.apply(hidden_states, shift_labels, weight_or_host_head, num_items_in_batch,
                                       v_chunk)

@@ -14,7 +14,7 @@ from dataclasses import dataclass
 
 import torch
 
-from .ops import V_CHUNK_DEFAULT, chunked_lm_head
+from .ops import chunked_lm_head
 from .proxy import ChunkedLogitsProxy
 
 IGNORE = -100
@@ -61,7 +61,7 @@ def scatter_head_outputs(packed: PackedBatch, nll: torch.Tensor, entropy: torch.
 
 
 def lm_head_with_proxy(hidden_packed: torch.Tensor, packed: PackedBatch, weight: torch.Tensor,
-                       num_items_in_batch=None, v_chunk: int = V_CHUNK_DEFAULT, proxy_dtype=torch.float16):
+                       num_items_in_batch=None, v_chunk: int | None = None, proxy_dtype=torch.float16):
     """Steps 3-4 of the reference's fused forward (ops.py:1143-1184): the head on packed
     hidden states, then a zero-storage [B, S, V] logits proxy. Returns (loss, proxy)."""
     loss, nll, ent, arg = chunked_lm_head(hidden_packed, packed.shift_labels, weight, num_items_in_batch, v_chunk)

@@ -30,8 +30,7 @@ import torch
 import torch.distributed as dist
 
 from . import _lib
-from .ops import (V_CHUNK_DEFAULT, _check_inputs, _stream, head_backward, head_backward_nvls, head_finish,
-                  head_forward_stats)
+from .ops import _check_inputs, _stream, head_backward, head_backward_nvls, head_finish, head_forward_stats
 
 
 def shard_range(vocab_size: int, rank: int, world: int) -> tuple[int, int]:
@@ -96,7 +95,7 @@ def nvls_dx_buffer(n: int, h: int, device: torch.device, group=None):
 class VocabShardedLMHeadFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, hidden_states, shift_labels, weight_shard, vocab_offset, vocab_size, group,
-                num_items_in_batch=None, v_chunk=V_CHUNK_DEFAULT):
+                num_items_in_batch=None, v_chunk=None):
         _check_inputs(hidden_states, shift_labels, weight_shard)
         h2d = hidden_states.contiguous().view(-1, hidden_states.shape[-1])
         labels = shift_labels.contiguous().view(-1).to(torch.int64)
@@ -114,7 +113,7 @@ class VocabShardedLMHeadFn(torch.autograd.Function):
         ctx.vocab_offset = int(vocab_offset)
         ctx.group = group
         ctx.orig_shape = hidden_states.shape
-        ctx.v_chunk = int(v_chunk) if v_chunk else V_CHUNK_DEFAULT
+        ctx.v_chunk = int(v_chunk) if v_chunk else 0
         ctx.mark_non_differentiable(nll, ent, arg)
         return loss, nll, ent, arg
 
@@ -154,7 +153,7 @@ class VocabShardedLMHeadFn(torch.autograd.Function):
 
 
 def sharded_lm_head(hidden_states, shift_labels, weight_shard, vocab_offset: int, vocab_size: int, group=None,
-                    num_items_in_batch=None, v_chunk: int = V_CHUNK_DEFAULT):
+                    num_items_in_batch=None, v_chunk: int | None = None):
     """Vocab-parallel ``chunked_lm_head``: same outputs on every rank; dW is the local shard's."""
     return VocabShardedLMHeadFn.apply(hidden_states, shift_labels, weight_shard, vocab_offset, vocab_size, group,
                                       num_items_in_batch, v_chunk)

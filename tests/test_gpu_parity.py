@@ -20,7 +20,7 @@ from oracle import lmce_oracle as orc
 pytestmark = pytest.mark.gpu
 
 
-def _run_ours(hidden, labels, weight, num_items=None, v_chunk=8192, want_dw=True):
+def _run_ours(hidden, labels, weight, num_items=None, v_chunk=None, want_dw=True):
     from rus_b200 import chunked_lm_head
 
     h = hidden.detach().clone().requires_grad_(True)
