@@ -135,9 +135,11 @@ LMCE_API int lmce_backward(const void* hidden, const void* weight, const int64_t
  * rank's copy while the remaining tiles compute. `d_hidden_multicast` must be
  * the multicast address of an fp32 [n_tokens, hidden_dim] buffer that every
  * rank of the group has zeroed before any rank starts this call (barrier), and
- * the ranks must synchronise again before reading the sum. Replaces the
- * reference-side gap of ops.py:320-338 (single GPU there) plus a separate
- * all-reduce. */
+ * the ranks must synchronise again before reading the sum. The reference is
+ * single-GPU (ops.py:320-338); this is the vocab-sharded form of its dX
+ * accumulation with the cross-GPU sum folded in instead of a separate
+ * all-reduce. The pointer must be a real multicast mapping (a multimem
+ * instruction on ordinary memory faults). */
 LMCE_API int lmce_backward_nvls(const void* hidden, const void* weight, const int64_t* labels, const float* lse,
                                 int64_t n_tokens, int64_t hidden_dim, int64_t vocab_local, int64_t vocab_offset,
                                 int dtype, const float* grad_loss, const float* denom, float* d_hidden_multicast,
