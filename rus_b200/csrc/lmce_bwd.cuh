@@ -60,6 +60,7 @@ struct BwdParams {
                            // the last chunk adds this rank's dX rows into it through the switch
   void* dw_out;            // [V][H] input dtype (nullable)
   int want_dx, want_dw;
+  int mn3_h;               // X and W MN-major maps are 3-D (H a multiple of 64, H >= 256); G's always are
   const float* grad_loss;  // device scalar (nullable: 1)
   const float* denom;      // device scalar
   float gscale;            // G prescale
@@ -365,10 +366,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             load_operand<BN>(sb, &map_wk, fb, false, t.chunk * p.v_chunk + t.n * BN, k0);
           } else if (t.kind == BK_DX) {
             load_operand<BM>(sa, &map_gk, fb, false, gbuf * p.rows_pad + t.m * BM, k0);
-            load_operand<BN>(sb, &map_wmn, fb, true, t.n * BN, t.chunk * p.v_chunk + k0);
+            if (p.mn3_h)
+              load_operand_mn3<BN>(sb, &map_wmn, fb, t.n * BN, t.chunk * p.v_chunk + k0);
+            else
+              load_operand<BN>(sb, &map_wmn, fb, true, t.n * BN, t.chunk * p.v_chunk + k0);
           } else {
-            load_operand<BM>(sa, &map_gmn, fb, true, t.m * BM, gbuf * p.rows_pad + k0);
-            load_operand<BN>(sb, &map_xmn, fb, true, t.n * BN, k0);
+            load_operand_mn3<BM>(sa, &map_gmn, fb, t.m * BM, gbuf * p.rows_pad + k0);
+            if (p.mn3_h)
+              load_operand_mn3<BN>(sb, &map_xmn, fb, t.n * BN, k0);
+            else
+              load_operand<BN>(sb, &map_xmn, fb, true, t.n * BN, k0);
           }
           ++issued;
           if (++stage == STAGES) {

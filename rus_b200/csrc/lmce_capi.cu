@@ -143,6 +143,27 @@ int make_map(CUtensorMap* m, const void* base, bool bf16, uint64_t inner, uint64
   return LMCE_OK;
 }
 
+// The same [outer][inner] tensor seen as 3-D for MN-major operands: {64 elements,
+// outer (the k rows), inner / 64 blocks of 64 elements at a 128-byte stride}, box
+// {64, 64, nblk}. One TMA instruction then fills nblk consecutive 8 KB swizzled
+// blocks, which is the layout the UMMA MN-major descriptor expects.
+int make_map_mn3(CUtensorMap* m, const void* base, bool bf16, uint64_t inner, uint64_t outer, uint64_t ld_elems,
+                 uint32_t nblk) {
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0) return fail(LMCE_ERR_INVALID_ARGUMENT, "tensor base not 16B aligned");
+  if ((ld_elems * 2) % 16 != 0) return fail(LMCE_ERR_INVALID_ARGUMENT, "row stride not a multiple of 16 bytes");
+  if (inner % 64 != 0) return fail(LMCE_ERR_INVALID_ARGUMENT, "3-D operand map needs a multiple of 64 columns");
+  cuuint64_t dims[3] = {64, outer, inner / 64};
+  cuuint64_t strides[2] = {ld_elems * 2, 128};
+  cuuint32_t box[3] = {64, 64, nblk};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                        const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(LMCE_ERR_CUDA, "cuTensorMapEncodeTiled (3-D) failed (%d)", static_cast<int>(r));
+  return LMCE_OK;
+}
+
 // ---------------------------------------------------------------- engines ---
 
 constexpr int kBN = BN;
@@ -735,12 +756,20 @@ int backward_impl(const void* hidden, const void* weight, const int64_t* labels,
   // [NUM_GBUF * rows_pad, v_chunk] tensor; buffer b starts at row b * rows_pad.
   CUtensorMap maps[6];  // x K-major, x MN-major, W K-major, W MN-major, G K-major, G MN-major
   const int g_rows = NUM_GBUF * L.rows_pad;
+  // MN-major operands load through 3-D maps (one TMA instruction per operand and k-block
+  // instead of one per 64 columns; the producer thread's issue rate bounds the DX and DW
+  // tiles otherwise). X and W fall back to 2-D maps when H is not a multiple of 64.
+  const bool mn3_h = h % 64 == 0 && h >= kBN;
   if (int rc = make_map(&maps[0], x_lab, bf16, h, L.rows_pad, h, BM)) return rc;
-  if (int rc = make_map(&maps[1], x_lab, bf16, h, L.rows_pad, h, 64)) return rc;
+  if (int rc = mn3_h ? make_map_mn3(&maps[1], x_lab, bf16, h, L.rows_pad, h, kBN / 64)
+                     : make_map(&maps[1], x_lab, bf16, h, L.rows_pad, h, 64))
+    return rc;
   if (int rc = make_map(&maps[2], weight, bf16, h, vl, h, kBN)) return rc;
-  if (int rc = make_map(&maps[3], weight, bf16, h, vl, h, 64)) return rc;
+  if (int rc = mn3_h ? make_map_mn3(&maps[3], weight, bf16, h, vl, h, kBN / 64)
+                     : make_map(&maps[3], weight, bf16, h, vl, h, 64))
+    return rc;
   if (int rc = make_map(&maps[4], g, bf16, L.v_chunk, g_rows, L.v_chunk, BM)) return rc;
-  if (int rc = make_map(&maps[5], g, bf16, L.v_chunk, g_rows, L.v_chunk, 64)) return rc;
+  if (int rc = make_map_mn3(&maps[5], g, bf16, L.v_chunk, g_rows, L.v_chunk, BM / 64)) return rc;
 
   int* sync = reinterpret_cast<int*>(ws + L.sync);
   LMCE_CUDA(cudaMemsetAsync(sync, 0, sizeof(int) * L.sync_ints, st));
@@ -763,6 +792,7 @@ int backward_impl(const void* hidden, const void* weight, const int64_t* labels,
   p.dw_out = d_weight;
   p.want_dx = want_dx ? 1 : 0;
   p.want_dw = want_dw ? 1 : 0;
+  p.mn3_h = mn3_h ? 1 : 0;
   p.grad_loss = grad_loss;
   p.denom = denom;
   p.gscale = 32768.0f;

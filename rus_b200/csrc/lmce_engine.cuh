@@ -139,6 +139,14 @@ __device__ __forceinline__ void load_operand(uint8_t* dst, const CUtensorMap* ma
   }
 }
 
+// MN-major operand through a 3-D tensor map (one TMA instruction for all ROWS / 64
+// blocks; same shared-memory image as load_operand with mn_major = true).
+template <int ROWS>
+__device__ __forceinline__ void load_operand_mn3(uint8_t* dst, const CUtensorMap* map, uint64_t* bar, int row0,
+                                                 int k0) {
+  tma_load_3d(dst, map, bar, 0, k0, row0 / 64);
+}
+
 // Descriptor of UMMA k-step k (K = 16) inside a staged operand. K-major: rows of
 // 128 bytes in 8-row swizzle atoms (SBO 1024), k advances 32 bytes within the row.
 // MN-major: K rows of 128 bytes (8-row groups, SBO 1024), 64-wide MN blocks
