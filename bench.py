@@ -360,9 +360,9 @@ def main():
     stage("report")
     dx_exchange = "none (single GPU)"
     if world > 1:
-        from rus_b200.sharded import nvls_dx_buffer
-        dx_exchange = ("in-kernel NVLink SHARP sum (multimem.red)" if nvls_dx_buffer(n_tokens, H, device, group)
-                       is not None else "NCCL all-reduce (fp32)")
+        from rus_b200.sharded import nvls_dx_exchange
+        dx_exchange = ("in-kernel NVLink SHARP exchange (multimem.ld_reduce + multimem.st)"
+                       if nvls_dx_exchange(n_tokens, H, dt, device, group) is not None else "NCCL all-reduce (fp32)")
     # ---- roofline of the dominant kernel (largest share of the step)
     peaks, peak_kind = load_peaks()
     v_local = v_hi - v_lo

@@ -128,23 +128,48 @@ LMCE_API int lmce_backward(const void* hidden, const void* weight, const int64_t
                   const float* grad_loss, const float* denom, void* d_hidden, float* d_hidden_f32,
                   void* d_weight, int64_t v_chunk, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Buffers of the cross-GPU dX sum that lmce_backward_nvls fuses into the
+ * backward of a vocab-sharded head. All three are allocations that every rank of
+ * the group has mapped into one NVLink multicast object (NVLink SHARP; e.g. torch
+ * symmetric memory): the *_mc fields are multicast addresses, the others this
+ * rank's own view. */
+typedef struct lmce_dx_exchange {
+  float* partial;          /* fp32 [n_tokens, hidden_dim]: this rank's dX contribution (scratch) */
+  const float* partial_mc; /* multicast address of `partial` */
+  void* out_mc;            /* dtype [n_tokens, hidden_dim]: on return every rank's copy holds the
+                              summed dX rows of the labelled tokens (other rows are not written) */
+  const uint32_t* flags;   /* uint32 [world + ceil(n_tokens / 128) * world * ceil(hidden_dim / 256)],
+                              zeroed on every rank (and a group barrier passed) before the first call */
+  uint32_t* flags_mc;      /* multicast address of `flags` */
+  uint32_t epoch;          /* 1 on the first call with these flags, then +1 per call; equal on all ranks */
+  int32_t rank, world;     /* this rank and the group size */
+} lmce_dx_exchange;
+
 /* lmce_backward for a vocab-sharded head with the cross-GPU dX sum fused into
- * the kernel: the dX rows of the last vocab chunk are added, as each tile
- * finishes, into `d_hidden_multicast` with NVLink SHARP reductions
- * (multimem.red), so the switch sums every rank's contribution into every
- * rank's copy while the remaining tiles compute. `d_hidden_multicast` must be
- * the multicast address of an fp32 [n_tokens, hidden_dim] buffer that every
- * rank of the group has zeroed before any rank starts this call (barrier), and
- * the ranks must synchronise again before reading the sum. The reference is
- * single-GPU (ops.py:320-338); this is the vocab-sharded form of its dX
- * accumulation with the cross-GPU sum folded in instead of a separate
- * all-reduce. The pointer must be a real multicast mapping (a multimem
- * instruction on ordinary memory faults). */
+ * the kernel. When a row block's last-chunk dX tiles are written (into
+ * xch->partial), the rank stamps their flags on every GPU (multimem.st of the
+ * epoch); rank r then sums its slice of the block's columns over all GPUs
+ * through the switch (multimem.ld_reduce) and stores the result to every GPU's
+ * output copy (multimem.st), while the last two vocab chunks' dW tiles still
+ * compute. Each GPU's NVLink traffic is about one fp32 read and one dtype write
+ * of dX, spread over the end of the kernel, instead of a separate all-reduce
+ * after it. Before the kernel ends it waits until every rank has finished its
+ * part, so when the call's stream work completes, the local copy of out_mc holds
+ * the sums (read it out with lmce_dx_copy_labelled) and the buffers may be reused
+ * by the next call, with epoch + 1. Every rank of the group makes every call with
+ * the same epoch. The waits for other ranks are bounded (LMCE_ERR_TIMEOUT through
+ * lmce_device_error). The reference is single-GPU (ops.py:320-338); this is the
+ * vocab-sharded form of its dX accumulation. */
 LMCE_API int lmce_backward_nvls(const void* hidden, const void* weight, const int64_t* labels, const float* lse,
                                 int64_t n_tokens, int64_t hidden_dim, int64_t vocab_local, int64_t vocab_offset,
-                                int dtype, const float* grad_loss, const float* denom, float* d_hidden_multicast,
+                                int dtype, const float* grad_loss, const float* denom, const lmce_dx_exchange* xch,
                                 void* d_weight, int64_t v_chunk, void* workspace, size_t workspace_bytes,
                                 void* stream);
+
+/* d_hidden[t] = src[t] for tokens whose label is not -100, zero rows otherwise
+ * ([n_tokens, hidden_dim] in dtype; the read-out of lmce_backward_nvls). */
+LMCE_API int lmce_dx_copy_labelled(const void* src, const int64_t* labels, int64_t n_tokens, int64_t hidden_dim,
+                                   int dtype, void* d_hidden, void* stream);
 
 /* d_hidden = dtype(d_hidden_f32), elementwise over n_tokens x hidden_dim. */
 LMCE_API int lmce_dx_finalize(const float* d_hidden_f32, int64_t n_tokens, int64_t hidden_dim, int dtype,

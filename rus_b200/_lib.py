@@ -25,6 +25,20 @@ LMCE_DTYPE_BF16 = 1
 
 PART_BYTES = 24  # sizeof(lmce_part)
 
+
+class DxExchange(ctypes.Structure):
+    """struct lmce_dx_exchange (buffers of the fused cross-GPU dX sum)."""
+    _fields_ = [
+        ("partial", ctypes.c_void_p),
+        ("partial_mc", ctypes.c_void_p),
+        ("out_mc", ctypes.c_void_p),
+        ("flags", ctypes.c_void_p),
+        ("flags_mc", ctypes.c_void_p),
+        ("epoch", ctypes.c_uint32),
+        ("rank", ctypes.c_int32),
+        ("world", ctypes.c_int32),
+    ]
+
 _ERR_NAMES = {
     LMCE_ERR_INVALID_ARGUMENT: "LMCE_ERR_INVALID_ARGUMENT",
     LMCE_ERR_UNSUPPORTED: "LMCE_ERR_UNSUPPORTED",
@@ -64,8 +78,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "lmce_backward_nvls": (
         _int,
-        [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _vp, _vp, _vp, _vp, _i64, _vp, ctypes.c_size_t, _vp],
+        [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, _vp, _vp, ctypes.POINTER(DxExchange), _vp, _i64, _vp,
+         ctypes.c_size_t, _vp],
     ),
+    "lmce_dx_copy_labelled": (_int, [_vp, _vp, _i64, _i64, _int, _vp, _vp]),
     "lmce_dx_finalize": (_int, [_vp, _i64, _i64, _int, _vp, _vp]),
     "lmce_selftest_wait_timeout": (_int, [ctypes.c_uint64, _vp]),
     "lmce_launch_count": (ctypes.c_uint64, []),

@@ -21,6 +21,20 @@
 //   read-modify-write of dX in chunk order (deterministic, no atomics on data).
 // A tile only waits for tiles earlier in the list, and tiles are claimed in list
 // order by running CTAs, so the earliest unfinished tile can always progress.
+//
+// Vocab-sharded runs over NVLink SHARP add a fourth kind, the cross-GPU dX sum:
+//   XCH(m, q)  rows of block m, columns piece q of this rank's slice of H: once every
+//              rank has written its last-chunk dX rows of block m, read the sum over
+//              the GPUs with multimem.ld_reduce and store it, in the input dtype, to
+//              every GPU's output copy with multimem.st.
+// The tail of the list then becomes DX(C-1) XCH DW(C-2) DW(C-1), so the exchange runs
+// while the last two chunks' dW tiles still compute. XCH waits only for DX tiles,
+// which every rank lists before its own XCH items, so no cycle between ranks exists.
+// Signals are words of a multicast flag array stamped with the call's epoch (so they
+// need no reset, whatever rows a call has): slot (m, rank, n) when DX(C-1) tile (m, n)
+// of that rank is written, and slot `rank` once all of the rank's XCH items are done.
+// Before the kernel ends, CTA 0 waits for every rank's done slot: then no GPU still
+// reads this rank's partials, and every GPU's sums have landed in this rank's copy.
 // Producers of a dependency publish with stores -> CTA barrier -> fence ->
 // atomic add; consumers acquire the counter, then fence the async proxy before
 // their TMA reads of G. Every wait is bounded.
@@ -32,11 +46,11 @@ namespace lmce {
 
 constexpr int NUM_GBUF = 3;
 constexpr int SCHED_DEPTH = 4;
-constexpr int DX_STAGE_LD = 36;                              // floats per staged row (32 + 4 pad)
-constexpr int DX_STAGE_BYTES = BM * DX_STAGE_LD * 4;          // 18 KB
-constexpr int BWD_SMEM_BYTES = TileCfg<false>::SMEM_BYTES + DX_STAGE_BYTES;
+constexpr int BWD_SMEM_BYTES = TileCfg<false>::SMEM_BYTES;
+constexpr int XCH_COLS = 256;   // columns of one exchange item
+constexpr int XCH_UNROLL = 4;   // independent 32-byte reductions in flight per thread
 
-enum : int { BK_END = -1, BK_G = 0, BK_DX = 1, BK_DW = 2 };
+enum : int { BK_END = -1, BK_G = 0, BK_DX = 1, BK_DW = 2, BK_XCH = 3 };
 
 struct BwdTile {
   int kind, chunk, m, n;
@@ -55,16 +69,24 @@ struct BwdParams {
   float* dx_acc;           // fp32 [rows_pad][H], compacted row order
   const int* row_idx;      // compacted row -> token row
   void* dx_out;            // [N][H] input dtype (nullable)
-  float* dx_out_f32;       // [N][H] fp32 (nullable; vocab-sharded runs)
-  float* dx_mc;            // multicast address of a zeroed fp32 [N][H] buffer on every rank (nullable):
-                           // the last chunk adds this rank's dX rows into it through the switch
+  float* dx_out_f32;       // [N][H] fp32 (nullable; vocab-sharded runs: this rank's contribution)
+  // fused cross-GPU dX sum (x_flags_mc == nullptr: off); dx_out_f32 is then the local
+  // view of the symmetric partial buffer whose multicast address is x_part_mc
+  const float* x_part_mc;  // multicast [N][H] fp32 partials
+  void* x_out_mc;          // multicast [N][H] input dtype: the sums
+  const uint32_t* x_flags; // local view of the flags: [world] done slots, then [m][world][num_hn] tile slots
+  uint32_t* x_flags_mc;    // multicast view of the flags
+  uint32_t x_epoch;        // stamp of this call (same on every rank)
+  int x_rank, x_world;
+  int x_lo, x_hi;          // this rank's column slice of H (multiples of 8)
   void* dw_out;            // [V][H] input dtype (nullable)
   int want_dx, want_dw;
   int mn3_h;               // X and W MN-major maps are 3-D (H a multiple of 64, H >= 256); G's always are
   const float* grad_loss;  // device scalar (nullable: 1)
   const float* denom;      // device scalar
   float gscale;            // G prescale
-  int* sync;               // zeroed: [0] ticket, [1..C] gdone, [1+C..2C] consumed, [1+2C..] dxchain
+  int* sync;               // zeroed: [0] ticket, [1..C] gdone, [1+C..2C] consumed, [1+2C..] dxchain,
+                           // then one count of this rank's finished XCH items
   int* err;
   unsigned long long timeout_ns;
 };
@@ -72,13 +94,14 @@ struct BwdParams {
 // Geometry derived from the parameters and the device-side labelled-token count
 // (identical in every thread of every CTA).
 struct BwdGeom {
-  int n_lab, num_m, num_hn, C, vc, V;
-  bool dx, dw;
+  int n_lab, num_m, num_hn, C, vc, V, nX;
+  bool dx, dw, xch;  // xch: the cross-GPU exchange is on (this rank may still own no XCH items)
   __device__ __forceinline__ int width(int c) const { return min(vc, V - c * vc); }
   __device__ __forceinline__ int nG(int c) const { return num_m * ((width(c) + BN - 1) / BN); }
   __device__ __forceinline__ int nDX() const { return dx ? num_m * num_hn : 0; }
   __device__ __forceinline__ int nDW(int c) const { return dw ? ((width(c) + BM - 1) / BM) * num_hn : 0; }
   __device__ __forceinline__ int num_kb(const BwdTile& t, int H) const {
+    if (t.kind == BK_XCH) return 0;
     if (t.kind == BK_G) return (H + BK - 1) / BK;
     if (t.kind == BK_DX) return (width(t.chunk) + BK - 1) / BK;
     return (n_lab + BK - 1) / BK;
@@ -95,6 +118,8 @@ __device__ __forceinline__ BwdGeom make_geom(const BwdParams& p) {
   g.V = p.V;
   g.dx = p.want_dx != 0;
   g.dw = p.want_dw != 0;
+  g.xch = p.x_flags_mc != nullptr && g.dx;
+  g.nX = g.xch ? g.num_m * ((p.x_hi - p.x_lo + XCH_COLS - 1) / XCH_COLS) : 0;
   return g;
 }
 
@@ -113,6 +138,30 @@ struct TileCursor {
   // kind, chunk, count and m-extent of segment `s`; false past the last segment
   __device__ __forceinline__ static bool segment(const BwdGeom& g, int s, int& kind, int& chunk, int& count,
                                                  int& mdim) {
+    if (g.xch) {
+      // exchange order: after DX(C-2) (after G(0) when C == 1): DX(C-1) XCH DW(C-2) DW(C-1)
+      const int head = g.C >= 2 ? 3 * g.C - 3 : 1;
+      if (s >= head) {
+        const int u = s - head;
+        chunk = g.C - 1;
+        mdim = g.num_m;
+        if (u == 0) {
+          kind = BK_DX;
+          count = g.nDX();
+        } else if (u == 1) {
+          kind = BK_XCH;
+          count = g.nX;
+        } else if (u <= 3) {
+          kind = BK_DW;
+          chunk = g.C - 4 + u;  // C-2, then C-1
+          count = chunk >= 0 ? g.nDW(chunk) : 0;
+          mdim = chunk >= 0 ? (g.width(chunk) + BM - 1) / BM : 1;
+        } else {
+          return false;
+        }
+        return true;
+      }
+    }
     if (s == 0) {
       kind = BK_G;
       chunk = 0;
@@ -198,6 +247,78 @@ __device__ __forceinline__ void publish_add(int* ctr, int v) {
   }
 }
 
+// Bounded wait until the word at f reaches stamp `target` (wrapping compare, system-scope acquire).
+__device__ __forceinline__ bool wait_flag_sys(const uint32_t* f, uint32_t target, volatile int* abort,
+                                              uint64_t limit_ns) {
+  if (static_cast<int>(ld_acquire_sys_u32(f) - target) >= 0) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (;;) {
+    __nanosleep(256);
+    if (static_cast<int>(ld_acquire_sys_u32(f) - target) >= 0) return true;
+    if (*abort) return false;
+    if (global_timer_ns() - t0 > limit_ns) return false;
+  }
+}
+
+// Exchange item XCH(m, q), run by the 128 epilogue threads: the cross-GPU sum of the
+// dX rows of block m over columns [c_lo, c_hi), written in the input dtype to every
+// GPU's output copy. Consecutive threads take consecutive 8-column groups of a row,
+// so each warp instruction covers contiguous bytes.
+template <bool BF16>
+__device__ __forceinline__ void exchange_rows(const BwdParams& p, const BwdGeom& geo, const BwdTile& t,
+                                              int* xdone, volatile int* abort_flag, uint64_t tlimit) {
+  const int et = static_cast<int>(threadIdx.x) - EPI_THREAD0;
+  // every rank's DX(C-1) tiles of row block m: one slot per thread
+  const int slots = p.x_world * geo.num_hn;
+  const uint32_t* tile_slots = p.x_flags + p.x_world + static_cast<size_t>(t.m) * slots;
+  for (int i = et; i < slots; i += EPI_THREADS) {
+    if (!wait_flag_sys(tile_slots + i, p.x_epoch, abort_flag, tlimit)) {
+      raise_error(p.err, ERR_TIMEOUT);
+      *abort_flag = 1;
+      break;
+    }
+  }
+  if (!epilogue_bar_all(*abort_flag == 0)) return;  // same decision in all 128 threads
+  const int c_lo = p.x_lo + t.n * XCH_COLS;
+  const int c_hi = min(c_lo + XCH_COLS, p.x_hi);
+  const int groups = (c_hi - c_lo) / 8;
+  const int rows = min(BM, geo.n_lab - t.m * BM);
+  const int total = rows * groups;
+  for (int base = 0; base < total; base += EPI_THREADS * XCH_UNROLL) {
+    float4 lo[XCH_UNROLL], hi[XCH_UNROLL];
+    long long off[XCH_UNROLL];
+#pragma unroll
+    for (int u = 0; u < XCH_UNROLL; ++u) {
+      const int i = base + u * EPI_THREADS + et;
+      off[u] = -1;
+      if (i < total) {
+        const int r = i / groups;
+        const int g = i - r * groups;
+        off[u] = static_cast<long long>(p.row_idx[t.m * BM + r]) * p.H + c_lo + g * 8;
+        lo[u] = multimem_ld_reduce_add_v4_f32(p.x_part_mc + off[u]);
+        hi[u] = multimem_ld_reduce_add_v4_f32(p.x_part_mc + off[u] + 4);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < XCH_UNROLL; ++u) {
+      if (off[u] >= 0)
+        multimem_st_v4_x2<BF16>(static_cast<char*>(p.x_out_mc) + off[u] * 2, pack2<BF16>(lo[u].x, lo[u].y),
+                                pack2<BF16>(lo[u].z, lo[u].w), pack2<BF16>(hi[u].x, hi[u].y),
+                                pack2<BF16>(hi[u].z, hi[u].w));
+    }
+  }
+  // the last of this rank's XCH items stamps the rank's done slot on every GPU
+  __threadfence_system();
+  epilogue_bar();
+  if (et == 0) {
+    const int prev = atomicAdd(xdone, 1);
+    if (prev + 1 == geo.nX) {
+      __threadfence_system();
+      multimem_st_release_b32(p.x_flags_mc + p.x_rank, p.x_epoch);
+    }
+  }
+}
+
 // UMMA k-loop of one tile. The operand majors and the instruction descriptor are
 // template constants: tcgen05.mma takes them from uniform registers, and values
 // that depend on the tile kind read from shared memory are not provably uniform
@@ -244,8 +365,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   BwdTile* ring = reinterpret_cast<BwdTile*>(sched_empty + SCHED_DEPTH);
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(ring + SCHED_DEPTH);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
-  // epilogue staging for the coalesced cross-GPU dX reduction (after the barrier block)
-  float* dx_stage = reinterpret_cast<float*>(smem + STAGES * C::STAGE_BYTES + 1024);
 
   const int warp = __shfl_sync(0xffffffffu, threadIdx.x / 32, 0);
   const int lane = threadIdx.x & 31;
@@ -254,6 +373,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   int* gdone = p.sync + 1;
   int* consumed = p.sync + 1 + p.n_chunks;
   int* dxchain = p.sync + 1 + 2 * p.n_chunks;
+  int* xdone = dxchain + (p.rows_pad / BM) * geo.num_hn;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -334,7 +454,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             ok = wait_counter(&consumed[prev], geo.nDX() + geo.nDW(prev), abort_flag, tlimit);
             if (ok) gbuf_free_chunk = t.chunk;
           }
-        } else {
+        } else if (t.kind != BK_XCH) {
           bool acquired = false;
           if (t.chunk > g_ready_chunk) {
             ok = wait_counter(&gdone[t.chunk], geo.nG(t.chunk), abort_flag, tlimit);
@@ -472,6 +592,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         sphase ^= 1u;
       }
       if (t.kind == BK_END) break;
+      if (t.kind == BK_XCH) {
+        if (!mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, tlimit)) {  // no UMMA: only keeps the slot order
+          ok = false;
+          break;
+        }
+        exchange_rows<BF16>(p, geo, t, xdone, abort_flag, tlimit);
+        mbar_arrive(&tempty_bar[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+        continue;
+      }
       const bool have_acc = geo.num_kb(t, p.H) > 0;
       const int w = geo.width(t.chunk);
       const int row = t.m * BM + r_in_tile;
@@ -555,30 +688,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               if (p.dx_out != nullptr) store32_dtype<BF16>(reinterpret_cast<char*>(p.dx_out) + (trow * p.H + col0) * 2, v);
             }
           }
-          if (p.dx_mc != nullptr && t.chunk + 1 == geo.C && col0 < p.H) {
-            // Cross-GPU sum of the finished dX rows through the switch. One thread per row would
-            // issue 32 scattered 16-byte reductions per warp instruction; staging the 128 x 32
-            // slice in shared memory lets each instruction cover 4 rows x 128 contiguous bytes.
-            float* stage_f = dx_stage + r_in_tile * DX_STAGE_LD;
-            const bool live = row < geo.n_lab;
-#pragma unroll
-            for (int j = 0; j < 32; j += 4)
-              *reinterpret_cast<float4*>(stage_f + j) =
-                  live ? make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]) : make_float4(0.f, 0.f, 0.f, 0.f);
-            epilogue_bar();
-            const int wq = (warp - 2) * 32;  // 32 staged rows handled by this warp
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const int r = wq + i * 4 + (lane >> 3);
-              const int grow = t.m * BM + r;
-              if (grow < geo.n_lab) {
-                const float4 f = *reinterpret_cast<const float4*>(dx_stage + r * DX_STAGE_LD + (lane & 7) * 4);
-                float* dst = p.dx_mc + static_cast<size_t>(p.row_idx[grow]) * p.H + col0 + (lane & 7) * 4;
-                multimem_red_add_v4_f32(dst, f.x, f.y, f.z, f.w);
-              }
-            }
-            epilogue_bar();
-          }
         } else {  // BK_DW
           if (row < w && col0 < p.H) {
 #pragma unroll
@@ -601,9 +710,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       } else if (t.kind == BK_DX) {
         epilogue_bar();
         if (threadIdx.x == EPI_THREAD0) {
-          __threadfence();
+          const bool x_last = geo.xch && t.chunk + 1 == geo.C;
+          if (x_last)
+            __threadfence_system();  // the partial rows are read by every GPU's exchange items
+          else
+            __threadfence();
           atomicAdd(&dxchain[t.m * geo.num_hn + t.n], 1);
           atomicAdd(&consumed[t.chunk], 1);
+          if (x_last)
+            multimem_st_release_b32(
+                p.x_flags_mc + p.x_world + (static_cast<size_t>(t.m) * p.x_world + p.x_rank) * geo.num_hn + t.n,
+                p.x_epoch);
         }
       } else {
         publish_add(&consumed[t.chunk], 1);
@@ -612,6 +729,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (!ok) {
       raise_error(p.err, ERR_TIMEOUT);
       *abort_flag = 1;
+    }
+    if (geo.xch && blockIdx.x == 0) {
+      // a rank without XCH items is done at once; then wait for every rank's done stamp
+      const int et = static_cast<int>(threadIdx.x) - EPI_THREAD0;
+      if (et == 0 && geo.nX == 0) multimem_st_release_b32(p.x_flags_mc + p.x_rank, p.x_epoch);
+      for (int r = et; r < p.x_world; r += EPI_THREADS) {
+        if (!*abort_flag && !wait_flag_sys(p.x_flags + r, p.x_epoch, abort_flag, tlimit)) {
+          raise_error(p.err, ERR_TIMEOUT);
+          *abort_flag = 1;
+        }
+      }
     }
   }
 

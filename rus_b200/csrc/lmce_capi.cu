@@ -507,6 +507,16 @@ __global__ void dx_finalize_kernel(const float4* __restrict__ src, long long n4,
   }
 }
 
+// dst row t = src row t for labelled tokens, zeros otherwise (rows of `vec` 16-byte units).
+__global__ void dx_copy_labelled_kernel(const uint4* __restrict__ src, const int64_t* __restrict__ labels, int vec,
+                                        long long total, uint4* __restrict__ dst) {
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long t = i / vec;
+    dst[i] = labels[t] != -100 ? src[i] : make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
 __global__ void selftest_wait_kernel(unsigned long long timeout_ns, int* err) {
   __shared__ uint64_t bar;
   __shared__ int abort_flag;
@@ -557,7 +567,7 @@ BwdLayout bwd_layout(int64_t n, int64_t h, int64_t v_local, int64_t v_chunk) {
   L.n_chunks = static_cast<int>((v_local + vc - 1) / vc);
   L.rows_pad = static_cast<int>((n + BM - 1) / BM * BM);
   const int num_hn = static_cast<int>((h + BN - 1) / BN);
-  L.sync_ints = 1 + 2 * L.n_chunks + (L.rows_pad / BM) * num_hn;
+  L.sync_ints = 1 + 2 * L.n_chunks + (L.rows_pad / BM) * num_hn + 1;
   size_t off = 0;
   L.count = off;
   off = align_up(off + 16, 256);
@@ -703,7 +713,7 @@ namespace {
 
 int backward_impl(const void* hidden, const void* weight, const int64_t* labels, const float* lse, int64_t n_tokens,
                   int64_t hidden_dim, int64_t vocab_local, int64_t vocab_offset, int dtype, const float* grad_loss,
-                  const float* denom, void* d_hidden, float* d_hidden_f32, float* d_hidden_mc, void* d_weight,
+                  const float* denom, void* d_hidden, float* d_hidden_f32, const lmce_dx_exchange* xch, void* d_weight,
                   int64_t v_chunk, void* workspace, size_t workspace_bytes, void* stream) {
   if (!hidden || !weight || !labels || !lse || !denom || !workspace)
     return fail(LMCE_ERR_INVALID_ARGUMENT, "null pointer");
@@ -713,9 +723,12 @@ int backward_impl(const void* hidden, const void* weight, const int64_t* labels,
   if (hidden_dim <= 0 || hidden_dim % 64 != 0) return fail(LMCE_ERR_UNSUPPORTED, "hidden_dim must be a positive multiple of 64");
   if (dtype != LMCE_DTYPE_F16 && dtype != LMCE_DTYPE_BF16) return fail(LMCE_ERR_UNSUPPORTED, "dtype %d", dtype);
   if ((d_hidden && !aligned16(d_hidden)) || (d_hidden_f32 && !aligned16(d_hidden_f32)) ||
-      (d_hidden_mc && !aligned16(d_hidden_mc)) ||
+      (xch && (!aligned16(xch->partial) || !aligned16(xch->partial_mc) || !aligned16(xch->out_mc))) ||
       (d_weight && !aligned16(d_weight)) || !aligned16(workspace))
     return fail(LMCE_ERR_INVALID_ARGUMENT, "output/workspace buffers must be 16-byte aligned");
+  if (xch && (!xch->partial || !xch->partial_mc || !xch->out_mc || !xch->flags || !xch->flags_mc ||
+              xch->world < 1 || xch->rank < 0 || xch->rank >= xch->world || xch->epoch == 0))
+    return fail(LMCE_ERR_INVALID_ARGUMENT, "bad dX exchange buffers");
   const BwdLayout L = bwd_layout(n_tokens, hidden_dim, vocab_local, v_chunk);
   if (workspace_bytes < L.total)
     return fail(LMCE_ERR_WORKSPACE, "workspace %zu bytes < required %zu", workspace_bytes, L.total);
@@ -748,7 +761,8 @@ int backward_impl(const void* hidden, const void* weight, const int64_t* labels,
     if (int rc = launched()) return rc;
   }
 
-  const bool want_dx = d_hidden != nullptr || d_hidden_f32 != nullptr || d_hidden_mc != nullptr;
+  if (xch) d_hidden_f32 = xch->partial;
+  const bool want_dx = d_hidden != nullptr || d_hidden_f32 != nullptr;
   const bool want_dw = d_weight != nullptr;
   if (!want_dx && !want_dw) return LMCE_OK;
 
@@ -788,7 +802,19 @@ int backward_impl(const void* hidden, const void* weight, const int64_t* labels,
   p.row_idx = row_idx;
   p.dx_out = d_hidden;
   p.dx_out_f32 = d_hidden_f32;
-  p.dx_mc = d_hidden_mc;
+  if (xch) {
+    // rank r sums columns [x_lo, x_hi) of every row block (8-column groups split evenly)
+    const int groups = h / 8;
+    p.x_part_mc = xch->partial_mc;
+    p.x_out_mc = xch->out_mc;
+    p.x_flags = xch->flags;
+    p.x_flags_mc = xch->flags_mc;
+    p.x_epoch = xch->epoch;
+    p.x_rank = xch->rank;
+    p.x_world = xch->world;
+    p.x_lo = groups * xch->rank / xch->world * 8;
+    p.x_hi = groups * (xch->rank + 1) / xch->world * 8;
+  }
   p.dw_out = d_weight;
   p.want_dx = want_dx ? 1 : 0;
   p.want_dw = want_dw ? 1 : 0;
@@ -817,12 +843,11 @@ int lmce_backward(const void* hidden, const void* weight, const int64_t* labels,
 
 int lmce_backward_nvls(const void* hidden, const void* weight, const int64_t* labels, const float* lse,
                        int64_t n_tokens, int64_t hidden_dim, int64_t vocab_local, int64_t vocab_offset, int dtype,
-                       const float* grad_loss, const float* denom, float* d_hidden_multicast, void* d_weight,
+                       const float* grad_loss, const float* denom, const lmce_dx_exchange* xch, void* d_weight,
                        int64_t v_chunk, void* workspace, size_t workspace_bytes, void* stream) {
-  if (d_hidden_multicast == nullptr) return fail(LMCE_ERR_INVALID_ARGUMENT, "null multicast dX buffer");
+  if (xch == nullptr) return fail(LMCE_ERR_INVALID_ARGUMENT, "null dX exchange descriptor");
   return backward_impl(hidden, weight, labels, lse, n_tokens, hidden_dim, vocab_local, vocab_offset, dtype, grad_loss,
-                       denom, nullptr, nullptr, d_hidden_multicast, d_weight, v_chunk, workspace, workspace_bytes,
-                       stream);
+                       denom, nullptr, nullptr, xch, d_weight, v_chunk, workspace, workspace_bytes, stream);
 }
 
 int lmce_dx_finalize(const float* d_hidden_f32, int64_t n_tokens, int64_t hidden_dim, int dtype, void* d_hidden,
@@ -845,6 +870,23 @@ int lmce_dx_finalize(const float* d_hidden_f32, int64_t n_tokens, int64_t hidden
         reinterpret_cast<const float4*>(d_hidden_f32), n4, static_cast<uint2*>(d_hidden));
   else
     return fail(LMCE_ERR_UNSUPPORTED, "dtype %d", dtype);
+  return launched();
+}
+
+int lmce_dx_copy_labelled(const void* src, const int64_t* labels, int64_t n_tokens, int64_t hidden_dim, int dtype,
+                          void* d_hidden, void* stream) {
+  if (!src || !labels || !d_hidden || n_tokens <= 0 || hidden_dim <= 0 || hidden_dim % 8 != 0)
+    return fail(LMCE_ERR_INVALID_ARGUMENT, "bad arguments");
+  if (dtype != LMCE_DTYPE_F16 && dtype != LMCE_DTYPE_BF16) return fail(LMCE_ERR_UNSUPPORTED, "dtype %d", dtype);
+  if (!aligned16(src) || !aligned16(d_hidden)) return fail(LMCE_ERR_INVALID_ARGUMENT, "misaligned buffers");
+  DevInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+  const int vec = static_cast<int>(hidden_dim * 2 / 16);
+  const long long total = n_tokens * vec;
+  long long blocks = (total + 255) / 256;
+  if (blocks > d->sms * 8ll) blocks = d->sms * 8ll;
+  dx_copy_labelled_kernel<<<static_cast<int>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(src), labels, vec, total, static_cast<uint4*>(d_hidden));
   return launched();
 }
 

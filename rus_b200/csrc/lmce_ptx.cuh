@@ -272,12 +272,42 @@ __device__ __forceinline__ void umma_commit_pair(uint32_t cluster_addr) {
 
 // --------------------------------------------------- NVLink SHARP reduction ---
 
-// out[0..3] += v on every GPU bound to the multicast address `mc` (the switch
-// reduces the contributions of all GPUs and writes the sum to each of them).
-__device__ __forceinline__ void multimem_red_add_v4_f32(float* mc, float a, float b, float c, float d) {
-  asm volatile("multimem.red.relaxed.sys.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc), "f"(a), "f"(b),
-               "f"(c), "f"(d)
+// NVLink SHARP (multimem) on a multicast address `mc`: the switch applies the
+// operation to the copy of every GPU bound to the multicast object.
+
+// Sum over all GPUs of the four floats at `mc` (the switch reads every copy and adds).
+__device__ __forceinline__ float4 multimem_ld_reduce_add_v4_f32(const float* mc) {
+  float4 r;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+               : "l"(mc)
                : "memory");
+  return r;
+}
+
+// Store 16 bytes (8 half or bfloat16 values, packed in pairs) to every GPU's copy.
+template <bool BF16>
+__device__ __forceinline__ void multimem_st_v4_x2(void* mc, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  if constexpr (BF16)
+    asm volatile("multimem.st.relaxed.sys.global.v4.bf16x2 [%0], {%1, %2, %3, %4};" ::"l"(mc), "r"(a), "r"(b),
+                 "r"(c), "r"(d)
+                 : "memory");
+  else
+    asm volatile("multimem.st.relaxed.sys.global.v4.f16x2 [%0], {%1, %2, %3, %4};" ::"l"(mc), "r"(a), "r"(b),
+                 "r"(c), "r"(d)
+                 : "memory");
+}
+
+// Every GPU's copy of the word at `mc` = v, ordered after this thread's earlier (and,
+// through a preceding barrier and fence, its CTA's) memory operations.
+__device__ __forceinline__ void multimem_st_release_b32(uint32_t* mc, uint32_t v) {
+  asm volatile("multimem.st.release.sys.global.b32 [%0], %1;" ::"l"(mc), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 
 // ------------------------------------------------------ UMMA descriptors ---

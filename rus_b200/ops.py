@@ -29,6 +29,7 @@ vocab-chunk gradient tile of N x v_chunk elements.
 """
 from __future__ import annotations
 
+import ctypes
 import os
 
 import torch
@@ -179,10 +180,12 @@ def head_backward(h2d, weight, labels, lse, grad_loss, denom, want_dx: bool, wan
     return dx, dw
 
 
-def head_backward_nvls(h2d, weight, labels, lse, grad_loss, denom, dx_multicast_ptr: int, want_dw: bool,
+def head_backward_nvls(h2d, weight, labels, lse, grad_loss, denom, xch, want_dw: bool,
                        v_chunk: int | None = None, vocab_offset: int = 0):
-    """Backward of one vocab shard whose dX rows are summed across the group inside the
-    kernel, into the multicast buffer at ``dx_multicast_ptr`` (lmce_backward_nvls)."""
+    """Backward of one vocab shard with the cross-GPU dX sum fused into the kernel
+    (lmce_backward_nvls); ``xch`` is the ``_lib.DxExchange`` of the group's symmetric
+    buffers. Returns this shard's dW (or None); the summed dX lands in every rank's
+    copy of ``xch.out_mc``."""
     n, h = h2d.shape
     v = weight.shape[0]
     dev = h2d.device
@@ -193,7 +196,7 @@ def head_backward_nvls(h2d, weight, labels, lse, grad_loss, denom, dx_multicast_
     dw = torch.empty_like(weight) if want_dw else None
     gl = grad_loss.detach().to(device=dev, dtype=torch.float32).reshape(1).contiguous()
     _lib.call("lmce_backward_nvls", h2d.data_ptr(), weight.data_ptr(), labels.data_ptr(), lse.data_ptr(), n, h, v,
-              vocab_offset, _DTYPES[h2d.dtype], gl.data_ptr(), denom.data_ptr(), dx_multicast_ptr, _ptr(dw),
+              vocab_offset, _DTYPES[h2d.dtype], gl.data_ptr(), denom.data_ptr(), ctypes.byref(xch), _ptr(dw),
               v_chunk, ws.data_ptr(), ws_bytes, _stream(dev))
     if _debug_sync():
         _raise_device_error()

@@ -8,16 +8,16 @@ hidden states and labels are replicated. The two exchange steps:
   (NCCL over NVLink, R x N x 24 bytes) and every rank merges them with
   ``lmce_stats_finish`` into identical lse / nll / entropy / argmax / loss.
 * backward: each rank contracts its shard's gradient tile into its local dW
-  shard and an fp32 dX contribution, which is summed over the ranks and cast to
-  the input dtype (``lmce_dx_finalize``). By default one NCCL all-reduce sums
-  the fp32 contributions. With ``LMCE_NVLS=1``, on GPUs that share an NVLink
-  switch with multicast (NVLS) support, the sum is fused into the backward
-  kernel instead: the last vocab chunk's dX tiles are added into a symmetric
-  multicast buffer with ``multimem.red`` as they finish (``lmce_backward_nvls``).
-  dX rows are final only once the last vocab chunk is done, so that sum runs at
-  the end of the kernel with little compute left to hide it; at the config-2
-  shape on 8 GPUs NCCL's all-reduce is faster (4.03 vs 4.66 ms per step), which
-  is why the fused path is opt-in.
+  shard and an fp32 dX contribution, which is summed over the ranks. With
+  ``LMCE_NVLS=1``, on GPUs that share an NVLink switch with multicast (NVLS)
+  support, the sum is fused into the backward kernel (``lmce_backward_nvls``):
+  as a row block's last-chunk dX tiles finish on every rank, each rank sums its
+  slice of the block's columns over the GPUs through the switch
+  (``multimem.ld_reduce``) and stores the result to every GPU's output copy
+  (``multimem.st``), while the last two chunks' dW tiles still compute. The
+  buffers are torch symmetric memory, allocated once per shape. Otherwise one
+  NCCL all-reduce sums the fp32 contributions after the kernel and
+  ``lmce_dx_finalize`` casts them to the input dtype.
 
 The reference has no multi-GPU path (it pins one T4); this is the B200 build's
 addition for the same operator interface.
@@ -62,34 +62,70 @@ def _group_name(group) -> str:
     return (group if group is not None else dist.group.WORLD).group_name
 
 
-def nvls_dx_buffer(n: int, h: int, device: torch.device, group=None):
-    """(fp32 [n, h] symmetric tensor, handle) with a multicast mapping on every rank of
-    the group, or None when the group cannot use NVLink SHARP (the decision is made
-    jointly, so every rank takes the same path). Cached per shape. Enabled by LMCE_NVLS=1."""
+class NvlsDxExchange:
+    """Symmetric buffers of the fused dX exchange for one (device, group, n, h, dtype):
+    the per-row-block flags, this rank's fp32 contribution and the dtype output, in one
+    allocation mapped into an NVLink multicast object on every rank of the group."""
+
+    def __init__(self, buf: torch.Tensor, hdl, n: int, h: int, dtype: torch.dtype, rank: int, world: int):
+        self.buf, self.hdl = buf, hdl
+        part_off = self.flag_bytes(n, h, world)
+        out_off = part_off + _round_up(4 * n * h, 256)
+        base, mc = buf.data_ptr(), int(hdl.multicast_ptr)
+        self.out_local = buf[out_off:out_off + 2 * n * h].view(dtype).view(n, h)
+        self.xch = _lib.DxExchange(partial=base + part_off, partial_mc=mc + part_off, out_mc=mc + out_off,
+                                   flags=base, flags_mc=mc, epoch=0, rank=rank, world=world)
+
+    @staticmethod
+    def flag_bytes(n: int, h: int, world: int) -> int:
+        # one done stamp per rank, then one stamp per (row block, rank, 256-column dX tile)
+        return _round_up(4 * (world + (n + 127) // 128 * world * ((h + 255) // 256)), 256)
+
+    @classmethod
+    def nbytes(cls, n: int, h: int, world: int) -> int:
+        return cls.flag_bytes(n, h, world) + _round_up(4 * n * h, 256) + _round_up(2 * n * h, 256)
+
+    def next_epoch(self) -> None:
+        self.xch.epoch = self.xch.epoch % 0xFFFFFFFF + 1
+
+
+def _round_up(x: int, a: int) -> int:
+    return (x + a - 1) // a * a
+
+
+def nvls_dx_exchange(n: int, h: int, dtype: torch.dtype, device: torch.device, group=None):
+    """The group's ``NvlsDxExchange`` for this shape, or None when the group cannot use
+    NVLink SHARP (the decision is made jointly, so every rank takes the same path).
+    Enabled by LMCE_NVLS=1; cached per shape."""
     if os.environ.get("LMCE_NVLS", "0") != "1" or device.type != "cuda":
         return None
-    key = (device.index, _group_name(group), n, h)
+    key = (device.index, _group_name(group), n, h, dtype)
     if key in _NVLS_CACHE:
         return _NVLS_CACHE[key]
-    buf = None
+    state = None
     ok = 1
     try:
         import torch.distributed._symmetric_memory as symm_mem
 
-        t = symm_mem.empty((n, h), dtype=torch.float32, device=device)
-        hdl = symm_mem.rendezvous(t, _group_name(group))
+        world = dist.get_world_size(group)
+        buf = symm_mem.empty(NvlsDxExchange.nbytes(n, h, world), dtype=torch.uint8, device=device)
+        hdl = symm_mem.rendezvous(buf, _group_name(group))
         if int(getattr(hdl, "multicast_ptr", 0)) == 0 or int(getattr(hdl, "offset", 0)) != 0:
             ok = 0
         else:
-            buf = (t, hdl)
+            state = NvlsDxExchange(buf, hdl, n, h, dtype, dist.get_rank(group), world)
     except Exception:
         ok = 0
     flag = torch.tensor([ok], dtype=torch.int32, device=device)
     dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
     if int(flag.item()) == 0:
-        buf = None
-    _NVLS_CACHE[key] = buf
-    return buf
+        state = None
+    else:
+        state.buf.zero_()  # flags start at zero on every rank before any rank's first call stamps them
+        torch.cuda.synchronize(device)
+        dist.barrier(group=group, device_ids=[device.index])
+    _NVLS_CACHE[key] = state
+    return state
 
 
 class VocabShardedLMHeadFn(torch.autograd.Function):
@@ -126,23 +162,24 @@ class VocabShardedLMHeadFn(torch.autograd.Function):
         dev = h2d.device
         n, h = h2d.shape
         with torch.cuda.device(dev):
-            nvls = nvls_dx_buffer(n, h, dev, ctx.group) if want_dx else None
+            nvls = nvls_dx_exchange(n, h, h2d.dtype, dev, ctx.group) if want_dx else None
             if nvls is not None:
-                # fused: the kernel adds this rank's dX rows into every rank's copy through the switch
-                dx_f32, hdl = nvls
-                dx_f32.zero_()
-                hdl.barrier(channel=0)  # every rank zeroed before any rank adds
-                dw = head_backward_nvls(h2d, w, labels, lse, grad_loss, denom, int(hdl.multicast_ptr), want_dw,
-                                        ctx.v_chunk, ctx.vocab_offset)
-                hdl.barrier(channel=0)  # every rank's additions have landed
-            else:
-                if want_dx:
-                    dx_f32 = torch.zeros(h2d.shape, dtype=torch.float32, device=dev)
-                # every rank takes the same collective steps, whatever it needs locally
-                _, dw = head_backward(h2d, w, labels, lse, grad_loss, denom, want_dx, want_dw, ctx.v_chunk,
-                                      vocab_offset=ctx.vocab_offset, dx_f32=dx_f32)
-                if want_dx:
-                    reduce_dx(dx_f32, ctx.group)
+                # fused: the kernel sums dX over the group through the switch into every rank's copy
+                # (the kernel returns only once every rank's sums have landed in this rank's copy)
+                nvls.next_epoch()
+                dw = head_backward_nvls(h2d, w, labels, lse, grad_loss, denom, nvls.xch, want_dw, ctx.v_chunk,
+                                        ctx.vocab_offset)
+                dx = torch.empty_like(h2d)
+                _lib.call("lmce_dx_copy_labelled", nvls.out_local.data_ptr(), labels.data_ptr(), n, h,
+                          0 if h2d.dtype == torch.float16 else 1, dx.data_ptr(), _stream(dev))
+                return dx.view(ctx.orig_shape), None, dw, None, None, None, None, None
+            if want_dx:
+                dx_f32 = torch.zeros(h2d.shape, dtype=torch.float32, device=dev)
+            # every rank takes the same collective steps, whatever it needs locally
+            _, dw = head_backward(h2d, w, labels, lse, grad_loss, denom, want_dx, want_dw, ctx.v_chunk,
+                                  vocab_offset=ctx.vocab_offset, dx_f32=dx_f32)
+            if want_dx:
+                reduce_dx(dx_f32, ctx.group)
             dx = None
             if want_dx:
                 dx = torch.empty_like(h2d)
