@@ -16,7 +16,7 @@ CSRC = PKG_DIR / "csrc"
 INCLUDE = PKG_DIR.parent / "include"
 LIB_PATH = PKG_DIR / "liblmce.so"
 SOURCES = [CSRC / "lmce_capi.cu"]
-DEPS = SOURCES + [CSRC / "lmce_engine.cuh", CSRC / "lmce_ptx.cuh", INCLUDE / "lmce.h"]
+DEPS = SOURCES + sorted(CSRC.glob("*.cuh")) + [INCLUDE / "lmce.h"]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -46,7 +46,11 @@ namespace lmce {
 
 constexpr int NUM_GBUF = 3;
 constexpr int SCHED_DEPTH = 4;
-constexpr int BWD_SMEM_BYTES = TileCfg<false>::SMEM_BYTES;
+// Per-warp staging of 32 rows x 32 columns of 16-bit output (64 bytes a row, padded to
+// 80 so the row-wise 16-byte writes of a warp hit distinct banks).
+constexpr int ROW_STAGE_PITCH = 80;
+constexpr int ROW_STAGE_BYTES = 4 * 32 * ROW_STAGE_PITCH;  // 10 KB for the four epilogue warps
+constexpr int BWD_SMEM_BYTES = TileCfg<false>::SMEM_BYTES + ROW_STAGE_BYTES;
 constexpr int XCH_COLS = 256;   // columns of one exchange item
 constexpr int XCH_UNROLL = 4;   // independent 32-byte reductions in flight per thread
 
@@ -247,6 +251,30 @@ __device__ __forceinline__ void publish_add(int* ctr, int v) {
   }
 }
 
+// Store a 32-row x 32-column block of 16-bit values held one row per lane (v = this
+// lane's 32 values) to rows [row0, row0 + 32) of a row-major tensor with `pitch`
+// elements per row, through the warp's staging slice: each store instruction then
+// covers 8 rows x 64 contiguous bytes instead of 32 rows x 16 bytes. Rows for which
+// `row_ok(r)` is false are not written. Called by all 32 lanes of the warp.
+template <bool BF16, typename RowOk>
+__device__ __forceinline__ void store_rows32(uint8_t* stage, const float* v, char* base, size_t pitch_bytes,
+                                             int row0, int lane, RowOk row_ok) {
+  uint4* mine = reinterpret_cast<uint4*>(stage + lane * ROW_STAGE_PITCH);
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    mine[q] = make_uint4(pack2<BF16>(v[8 * q + 0], v[8 * q + 1]), pack2<BF16>(v[8 * q + 2], v[8 * q + 3]),
+                         pack2<BF16>(v[8 * q + 4], v[8 * q + 5]), pack2<BF16>(v[8 * q + 6], v[8 * q + 7]));
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = i * 8 + (lane >> 2);
+    const int piece = lane & 3;
+    const uint4 u = *reinterpret_cast<const uint4*>(stage + r * ROW_STAGE_PITCH + piece * 16);
+    if (row_ok(row0 + r)) *reinterpret_cast<uint4*>(base + static_cast<size_t>(row0 + r) * pitch_bytes + piece * 16) = u;
+  }
+  __syncwarp();
+}
+
 // Bounded wait until the word at f reaches stamp `target` (wrapping compare, system-scope acquire).
 __device__ __forceinline__ bool wait_flag_sys(const uint32_t* f, uint32_t target, volatile int* abort,
                                               uint64_t limit_ns) {
@@ -368,6 +396,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   const int warp = __shfl_sync(0xffffffffu, threadIdx.x / 32, 0);
   const int lane = threadIdx.x & 31;
+  // epilogue row staging (after the barrier block); warp quadrant q uses slice q
+  uint8_t* row_stage = smem + STAGES * C::STAGE_BYTES + 1024 + (warp & 3) * 32 * ROW_STAGE_PITCH;
   const BwdGeom geo = make_geom(p);
   int* ticket = p.sync;
   int* gdone = p.sync + 1;
@@ -655,9 +685,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             if (static_cast<unsigned>(j) == rel) pr -= 1.0f;
             v[j] = (g_row_ok && col0 + j < w) ? pr * p.gscale : 0.0f;
           }
-          char* dst = reinterpret_cast<char*>(p.g) +
-                      ((static_cast<size_t>(t.chunk % NUM_GBUF) * p.rows_pad + row) * p.v_chunk + col0) * 2;
-          store32_dtype<BF16>(dst, v);
+          char* gbase = reinterpret_cast<char*>(p.g) +
+                        (static_cast<size_t>(t.chunk % NUM_GBUF) * p.rows_pad * p.v_chunk + col0) * 2;
+          store_rows32<BF16>(row_stage, v, gbase, static_cast<size_t>(p.v_chunk) * 2, t.m * BM + q * 32, lane,
+                             [](int) { return true; });
         } else if (t.kind == BK_DX) {
           if (row < geo.n_lab && col0 < p.H) {
 #pragma unroll
@@ -689,12 +720,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
           }
         } else {  // BK_DW
-          if (row < w && col0 < p.H) {
+          if (col0 < p.H) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] *= dscale;
-            char* dst = reinterpret_cast<char*>(p.dw_out) +
-                        ((static_cast<size_t>(t.chunk) * p.v_chunk + row) * p.H + col0) * 2;
-            store32_dtype<BF16>(dst, v);
+            char* dbase = reinterpret_cast<char*>(p.dw_out) +
+                          (static_cast<size_t>(t.chunk) * p.v_chunk * p.H + col0) * 2;
+            store_rows32<BF16>(row_stage, v, dbase, static_cast<size_t>(p.H) * 2, t.m * BM + q * 32, lane,
+                               [w](int r) { return r < w; });
           }
         }
       }
