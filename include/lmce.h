@@ -138,7 +138,7 @@ typedef struct lmce_dx_exchange {
   const float* partial_mc; /* multicast address of `partial` */
   void* out_mc;            /* dtype [n_tokens, hidden_dim]: on return every rank's copy holds the
                               summed dX rows of the labelled tokens (other rows are not written) */
-  const uint32_t* flags;   /* uint32 [world + ceil(n_tokens / 128) * world * ceil(hidden_dim / 256)],
+  const uint32_t* flags;   /* uint32 [world + 2 * ceil(n_tokens / 256) * world * ceil(hidden_dim / 256)],
                               zeroed on every rank (and a group barrier passed) before the first call */
   uint32_t* flags_mc;      /* multicast address of `flags` */
   uint32_t epoch;          /* 1 on the first call with these flags, then +1 per call; equal on all ranks */

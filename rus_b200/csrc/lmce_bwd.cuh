@@ -288,29 +288,33 @@ __device__ __forceinline__ bool wait_flag_sys(const uint32_t* f, uint32_t target
   }
 }
 
-// Exchange item XCH(m, q), run by the 128 epilogue threads: the cross-GPU sum of the
-// dX rows of block m over columns [c_lo, c_hi), written in the input dtype to every
-// GPU's output copy. Consecutive threads take consecutive 8-column groups of a row,
-// so each warp instruction covers contiguous bytes.
-template <bool BF16>
-__device__ __forceinline__ void exchange_rows(const BwdParams& p, const BwdGeom& geo, const BwdTile& t,
-                                              int* xdone, volatile int* abort_flag, uint64_t tlimit) {
+// Exchange item XCH(m, q), run by the 128 epilogue threads: the cross-GPU sum of
+// dX rows [row0, row0 + 128) of row block m (clipped to n_lab) over columns
+// [c_lo, c_hi), written in the input dtype to every GPU's output copy. It starts once
+// every rank stamped the `stamps` flag slots it owns for block m (one per DX tile
+// half that covers the block). Consecutive threads take consecutive 8-column groups
+// of a row, so each warp instruction covers contiguous bytes. The call that brings
+// this GPU's count of finished items to `items` stamps the GPU's done slot. Run by the
+// 128 threads EPI_THREAD0 .. EPI_THREAD0 + 127, which synchronise on named barrier BAR.
+template <bool BF16, int BAR>
+__device__ __forceinline__ void exchange_rows_range(const BwdParams& p, int row0, int n_lab, int stamps,
+                                                    const BwdTile& t, int* xdone, int items, volatile int* abort_flag,
+                                                    uint64_t tlimit) {
   const int et = static_cast<int>(threadIdx.x) - EPI_THREAD0;
-  // every rank's DX(C-1) tiles of row block m: one slot per thread
-  const int slots = p.x_world * geo.num_hn;
-  const uint32_t* tile_slots = p.x_flags + p.x_world + static_cast<size_t>(t.m) * slots;
+  const int slots = p.x_world * stamps;
+  const uint32_t* block_slots = p.x_flags + p.x_world + static_cast<size_t>(t.m) * slots;
   for (int i = et; i < slots; i += EPI_THREADS) {
-    if (!wait_flag_sys(tile_slots + i, p.x_epoch, abort_flag, tlimit)) {
+    if (!wait_flag_sys(block_slots + i, p.x_epoch, abort_flag, tlimit)) {
       raise_error(p.err, ERR_TIMEOUT);
       *abort_flag = 1;
       break;
     }
   }
-  if (!epilogue_bar_all(*abort_flag == 0)) return;  // same decision in all 128 threads
+  if (!named_bar_all<BAR, EPI_THREADS>(*abort_flag == 0)) return;  // same decision in all 128 threads
   const int c_lo = p.x_lo + t.n * XCH_COLS;
   const int c_hi = min(c_lo + XCH_COLS, p.x_hi);
   const int groups = (c_hi - c_lo) / 8;
-  const int rows = min(BM, geo.n_lab - t.m * BM);
+  const int rows = max(0, min(BM, n_lab - row0));
   const int total = rows * groups;
   for (int base = 0; base < total; base += EPI_THREADS * XCH_UNROLL) {
     float4 lo[XCH_UNROLL], hi[XCH_UNROLL];
@@ -322,7 +326,7 @@ __device__ __forceinline__ void exchange_rows(const BwdParams& p, const BwdGeom&
       if (i < total) {
         const int r = i / groups;
         const int g = i - r * groups;
-        off[u] = static_cast<long long>(p.row_idx[t.m * BM + r]) * p.H + c_lo + g * 8;
+        off[u] = static_cast<long long>(p.row_idx[row0 + r]) * p.H + c_lo + g * 8;
         lo[u] = multimem_ld_reduce_add_v4_f32(p.x_part_mc + off[u]);
         hi[u] = multimem_ld_reduce_add_v4_f32(p.x_part_mc + off[u] + 4);
       }
@@ -335,12 +339,11 @@ __device__ __forceinline__ void exchange_rows(const BwdParams& p, const BwdGeom&
                                 pack2<BF16>(hi[u].z, hi[u].w));
     }
   }
-  // the last of this rank's XCH items stamps the rank's done slot on every GPU
   __threadfence_system();
-  epilogue_bar();
+  named_bar<BAR, EPI_THREADS>();
   if (et == 0) {
     const int prev = atomicAdd(xdone, 1);
-    if (prev + 1 == geo.nX) {
+    if (prev + 1 == items) {
       __threadfence_system();
       multimem_st_release_b32(p.x_flags_mc + p.x_rank, p.x_epoch);
     }
@@ -627,7 +630,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           ok = false;
           break;
         }
-        exchange_rows<BF16>(p, geo, t, xdone, abort_flag, tlimit);
+        exchange_rows_range<BF16, 1>(p, t.m * BM, geo.n_lab, geo.num_hn, t, xdone, geo.nX, abort_flag, tlimit);
         mbar_arrive(&tempty_bar[acc]);
         if (++acc == 2) {
           acc = 0;

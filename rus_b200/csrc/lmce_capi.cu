@@ -16,6 +16,7 @@
 
 #include "../../include/lmce.h"
 #include "lmce_bwd.cuh"
+#include "lmce_bwd_pair.cuh"
 
 using namespace lmce;
 
@@ -183,10 +184,11 @@ int ensure_smem_attr(K kern, int smem, bool* done) {
 
 // Launch with an optional cluster of 2 CTAs (pair kernels).
 template <typename... KArgs, typename... Args>
-int launch_ex(void (*kern)(KArgs...), int grid, int smem, int cluster, cudaStream_t st, Args&&... args) {
+int launch_ex(void (*kern)(KArgs...), int grid, int threads, int smem, int cluster, cudaStream_t st,
+              Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid, 1, 1);
-  cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+  cfg.blockDim = dim3(threads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -203,13 +205,13 @@ int launch_ex(void (*kern)(KArgs...), int grid, int smem, int cluster, cudaStrea
 
 // Co-resident clusters of the pair kernel `kern` on the current device (cached per device and kernel).
 template <typename K>
-int max_pairs(K kern, int smem, int sms, int* cache) {
+int max_pairs(K kern, int smem, int sms, int* cache, int threads = NUM_THREADS) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return sms / 2;
   if (cache[dev] > 0) return cache[dev];
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(sms, 1, 1);
-  cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+  cfg.blockDim = dim3(threads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -231,7 +233,7 @@ int launch_stats(const CUtensorMap& mx, const CUtensorMap& mw, const StatsParams
   static bool done[kMaxDevices] = {};
   if (int rc = ensure_smem_attr(kern, smem, done)) return rc;
   timing_mark(0, 0, st);
-  const int rc = launch_ex(kern, grid, smem, PAIR ? 2 : 1, st, mx, mw, p);
+  const int rc = launch_ex(kern, grid, NUM_THREADS, smem, PAIR ? 2 : 1, st, mx, mw, p);
   timing_mark(0, 1, st);
   return rc;
 }
@@ -267,6 +269,35 @@ int launch_bwd(const CUtensorMap* maps, const BwdParams& p, int grid, cudaStream
   const int rc = launched();
   timing_mark(1, 1, st);
   return rc;
+}
+
+// Backward on CTA pairs: one cluster of two per pair of SMs that can be co-resident.
+template <bool BF16>
+int launch_bwd_pair(const CUtensorMap* maps, const BwdParams& p, int sms, cudaStream_t st) {
+  auto kern = lmce_bwd_pair_kernel<BF16>;
+  constexpr int smem = PBWD_SMEM_BYTES;
+  static bool done[kMaxDevices] = {};
+  static int pairs_cache[kMaxDevices] = {};
+  if (int rc = ensure_smem_attr(kern, smem, done)) return rc;
+  const int pairs = max_pairs(kern, smem, sms, pairs_cache, P_THREADS);
+  timing_mark(1, 0, st);
+  const int rc =
+      launch_ex(kern, 2 * pairs, P_THREADS, smem, 2, st, maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], p);
+  timing_mark(1, 1, st);
+  return rc;
+}
+
+// Which backward kernel runs: the CTA-pair kernel needs H >= 256 (3-D operand maps);
+// LMCE_BWD_KERNEL=single forces the one-CTA kernel.
+bool use_pair_backward(int64_t h) {
+  static const int forced = [] {
+    const char* e = std::getenv("LMCE_BWD_KERNEL");
+    if (e && std::strcmp(e, "single") == 0) return 1;
+    if (e && std::strcmp(e, "pair") == 0) return 2;
+    return 0;
+  }();
+  if (h % 64 != 0 || h < kBN) return false;
+  return forced != 1;
 }
 
 // Vocab slabs per token block: fill the SMs with whole waves of (block, slab)
@@ -565,7 +596,7 @@ BwdLayout bwd_layout(int64_t n, int64_t h, int64_t v_local, int64_t v_chunk) {
   if (vc < 256) vc = 256;
   L.v_chunk = static_cast<int>(vc);
   L.n_chunks = static_cast<int>((v_local + vc - 1) / vc);
-  L.rows_pad = static_cast<int>((n + BM - 1) / BM * BM);
+  L.rows_pad = static_cast<int>((n + 255) / 256 * 256);  // row blocks of 256 (pair kernel), 128 (one-CTA)
   const int num_hn = static_cast<int>((h + BN - 1) / BN);
   L.sync_ints = 1 + 2 * L.n_chunks + (L.rows_pad / BM) * num_hn + 1;
   size_t off = 0;
@@ -768,22 +799,36 @@ int backward_impl(const void* hidden, const void* weight, const int64_t* labels,
 
   // Tensor maps (tile offsets are TMA coordinates). The three G buffers are one
   // [NUM_GBUF * rows_pad, v_chunk] tensor; buffer b starts at row b * rows_pad.
-  CUtensorMap maps[6];  // x K-major, x MN-major, W K-major, W MN-major, G K-major, G MN-major
-  const int g_rows = NUM_GBUF * L.rows_pad;
   // MN-major operands load through 3-D maps (one TMA instruction per operand and k-block
   // instead of one per 64 columns; the producer thread's issue rate bounds the DX and DW
-  // tiles otherwise). X and W fall back to 2-D maps when H is not a multiple of 64.
+  // tiles otherwise).
+  CUtensorMap maps[6];
+  const int g_rows = NUM_GBUF * L.rows_pad;
+  const bool pair = use_pair_backward(h);
   const bool mn3_h = h % 64 == 0 && h >= kBN;
-  if (int rc = make_map(&maps[0], x_lab, bf16, h, L.rows_pad, h, BM)) return rc;
-  if (int rc = mn3_h ? make_map_mn3(&maps[1], x_lab, bf16, h, L.rows_pad, h, kBN / 64)
-                     : make_map(&maps[1], x_lab, bf16, h, L.rows_pad, h, 64))
-    return rc;
-  if (int rc = make_map(&maps[2], weight, bf16, h, vl, h, kBN)) return rc;
-  if (int rc = mn3_h ? make_map_mn3(&maps[3], weight, bf16, h, vl, h, kBN / 64)
-                     : make_map(&maps[3], weight, bf16, h, vl, h, 64))
-    return rc;
-  if (int rc = make_map(&maps[4], g, bf16, L.v_chunk, g_rows, L.v_chunk, BM)) return rc;
-  if (int rc = make_map_mn3(&maps[5], g, bf16, L.v_chunk, g_rows, L.v_chunk, BM / 64)) return rc;
+  if (pair) {
+    // W K-major, W MN-major, X K-major, X MN-major, G K-major, G MN-major; every box is
+    // one CTA's half of a pair tile (128 rows, or two 64-column MN blocks)
+    if (int rc = make_map(&maps[0], weight, bf16, h, vl, h, BM)) return rc;
+    if (int rc = make_map_mn3(&maps[1], weight, bf16, h, vl, h, BM / 64)) return rc;
+    if (int rc = make_map(&maps[2], x_lab, bf16, h, L.rows_pad, h, BM)) return rc;
+    if (int rc = make_map_mn3(&maps[3], x_lab, bf16, h, L.rows_pad, h, BM / 64)) return rc;
+    if (int rc = make_map(&maps[4], g, bf16, L.v_chunk, g_rows, L.v_chunk, BM)) return rc;
+    if (int rc = make_map_mn3(&maps[5], g, bf16, L.v_chunk, g_rows, L.v_chunk, BM / 64)) return rc;
+  } else {
+    // x K-major, x MN-major, W K-major, W MN-major, G K-major, G MN-major (X and W fall
+    // back to 2-D MN-major maps when H is below 256)
+    if (int rc = make_map(&maps[0], x_lab, bf16, h, L.rows_pad, h, BM)) return rc;
+    if (int rc = mn3_h ? make_map_mn3(&maps[1], x_lab, bf16, h, L.rows_pad, h, kBN / 64)
+                       : make_map(&maps[1], x_lab, bf16, h, L.rows_pad, h, 64))
+      return rc;
+    if (int rc = make_map(&maps[2], weight, bf16, h, vl, h, kBN)) return rc;
+    if (int rc = mn3_h ? make_map_mn3(&maps[3], weight, bf16, h, vl, h, kBN / 64)
+                       : make_map(&maps[3], weight, bf16, h, vl, h, 64))
+      return rc;
+    if (int rc = make_map(&maps[4], g, bf16, L.v_chunk, g_rows, L.v_chunk, BM)) return rc;
+    if (int rc = make_map_mn3(&maps[5], g, bf16, L.v_chunk, g_rows, L.v_chunk, BM / 64)) return rc;
+  }
 
   int* sync = reinterpret_cast<int*>(ws + L.sync);
   LMCE_CUDA(cudaMemsetAsync(sync, 0, sizeof(int) * L.sync_ints, st));
@@ -826,6 +871,7 @@ int backward_impl(const void* hidden, const void* weight, const int64_t* labels,
   p.err = d->err_ptr;
   p.timeout_ns = wait_timeout_ns();
   const int grid = d->sms;
+  if (pair) return bf16 ? launch_bwd_pair<true>(maps, p, grid, st) : launch_bwd_pair<false>(maps, p, grid, st);
   return bf16 ? launch_bwd<true>(maps, p, grid, st) : launch_bwd<false>(maps, p, grid, st);
 }
 

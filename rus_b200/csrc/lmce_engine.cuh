@@ -90,6 +90,20 @@ __device__ __forceinline__ float round_to_input(float x) {
   }
 }
 
+// x rounded to the significand width of the input dtype (11 bits for fp16, 8 for
+// bf16) on the FP32 pipe: Veltkamp's split, hi = t - (t - x) with t = x * (2^s + 1),
+// s = 24 - width, keeps the leading bits of x rounded to nearest (T. J. Dekker, "A
+// floating-point technique for extending the available precision", 1971). Against
+// round_to_input it can differ only on exact ties and below the fp16 normal range,
+// and it never overflows to inf; the backward's G uses it, since two conversions per
+// logit would bound its epilogue by the conversion unit's rate.
+template <bool BF16>
+__device__ __forceinline__ float round_split(float x) {
+  constexpr float c = BF16 ? 65537.0f : 8193.0f;
+  const float t = __fmul_rn(x, c);
+  return __fsub_rn(t, __fsub_rn(t, x));
+}
+
 template <bool BF16>
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
   if constexpr (BF16) {
@@ -122,6 +136,27 @@ __device__ __forceinline__ void raise_error(int* err, int code) {
 
 // Named barrier over the 128 epilogue threads (warps 2..5); barrier 0 is __syncthreads.
 __device__ __forceinline__ void epilogue_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// Named barrier ID among COUNT threads (the epilogue warps of a kernel, or a subset).
+template <int ID, int COUNT>
+__device__ __forceinline__ void named_bar() {
+  asm volatile("bar.sync %0, %1;" ::"n"(ID), "n"(COUNT) : "memory");
+}
+
+// named_bar that also returns the AND of `pred` over its COUNT threads (one answer for all).
+template <int ID, int COUNT>
+__device__ __forceinline__ bool named_bar_all(bool pred) {
+  uint32_t out;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\t"
+      "setp.ne.u32 pi, %1, 0;\n\t"
+      "bar.red.and.pred po, %2, %3, pi;\n\t"
+      "selp.u32 %0, 1, 0, po;\n\t}"
+      : "=r"(out)
+      : "r"(static_cast<uint32_t>(pred)), "n"(ID), "n"(COUNT)
+      : "memory");
+  return out != 0;
+}
 
 // Epilogue barrier that also returns the AND of `pred` over the 128 threads (one answer for all).
 __device__ __forceinline__ bool epilogue_bar_all(bool pred) {

@@ -78,8 +78,9 @@ class NvlsDxExchange:
 
     @staticmethod
     def flag_bytes(n: int, h: int, world: int) -> int:
-        # one done stamp per rank, then one stamp per (row block, rank, 256-column dX tile)
-        return _round_up(4 * (world + (n + 127) // 128 * world * ((h + 255) // 256)), 256)
+        # one done stamp per rank, then per 256-row block, rank and 256-column dX tile two
+        # stamps (the two 128-row blocks of the one-CTA kernel, or the pair kernel's halves)
+        return _round_up(4 * (world + 2 * ((n + 255) // 256) * world * ((h + 255) // 256)), 256)
 
     @classmethod
     def nbytes(cls, n: int, h: int, world: int) -> int:
