@@ -8,16 +8,19 @@ hidden states and labels are replicated. The two exchange steps:
   (NCCL over NVLink, R x N x 24 bytes) and every rank merges them with
   ``lmce_stats_finish`` into identical lse / nll / entropy / argmax / loss.
 * backward: each rank contracts its shard's gradient tile into its local dW
-  shard and an fp32 dX contribution, which is summed over the ranks. With
-  ``LMCE_NVLS=1``, on GPUs that share an NVLink switch with multicast (NVLS)
-  support, the sum is fused into the backward kernel (``lmce_backward_nvls``):
+  shard and an fp32 dX contribution, which is summed over the ranks. On GPUs
+  that share an NVLink switch with multicast (NVLS) support, for dX of at least
+  64 MiB in fp32 (``LMCE_NVLS=1`` forces it, ``0`` disables it), the sum is
+  fused into the backward kernel (``lmce_backward_nvls``):
   as a row block's last-chunk dX tiles finish on every rank, each rank sums its
   slice of the block's columns over the GPUs through the switch
   (``multimem.ld_reduce``) and stores the result to every GPU's output copy
   (``multimem.st``), while the last two chunks' dW tiles still compute. The
   buffers are torch symmetric memory, allocated once per shape. Otherwise one
   NCCL all-reduce sums the fp32 contributions after the kernel and
-  ``lmce_dx_finalize`` casts them to the input dtype.
+  ``lmce_dx_finalize`` casts them to the input dtype. Measured on 8 B200s at the
+  config-2 shape: 3.58 ms per step fused against 3.90 with NCCL for 16384 tokens
+  (dX 100 MB); 0.84 against 0.80 ms for 2048 tokens (12.6 MB), hence the size rule.
 
 The reference has no multi-GPU path (it pins one T4); this is the B200 build's
 addition for the same operator interface.
@@ -94,11 +97,18 @@ def _round_up(x: int, a: int) -> int:
     return (x + a - 1) // a * a
 
 
+NVLS_MIN_DX_BYTES = 64 << 20  # fp32 dX size from which the fused exchange beats NCCL's all-reduce
+
+
 def nvls_dx_exchange(n: int, h: int, dtype: torch.dtype, device: torch.device, group=None):
-    """The group's ``NvlsDxExchange`` for this shape, or None when the group cannot use
-    NVLink SHARP (the decision is made jointly, so every rank takes the same path).
-    Enabled by LMCE_NVLS=1; cached per shape."""
-    if os.environ.get("LMCE_NVLS", "0") != "1" or device.type != "cuda":
+    """The group's ``NvlsDxExchange`` for this shape, or None when the fused exchange is
+    not used: LMCE_NVLS=0, or (default) fp32 dX below NVLS_MIN_DX_BYTES, or the group
+    cannot use NVLink SHARP (decided jointly, so every rank takes the same path).
+    LMCE_NVLS=1 uses it whenever the GPUs support it. Cached per shape."""
+    mode = os.environ.get("LMCE_NVLS", "auto")
+    if mode == "0" or device.type != "cuda":
+        return None
+    if mode != "1" and 4 * n * h < NVLS_MIN_DX_BYTES:
         return None
     key = (device.index, _group_name(group), n, h, dtype)
     if key in _NVLS_CACHE:
