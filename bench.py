@@ -43,9 +43,9 @@ CONFIGS = {
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM bytes (read + write) of one forward-statistics launch at config 2, from
 # one `ncu --set full` capture (profiles/lmce_head_c2_fwd_bwd.md).
-FWD_STATS_TRAFFIC_C2 = 504_142_000 + 5_926_000
-# DRAM bytes of one persistent backward launch at config 2 (same profile file).
-BWD_TRAFFIC_C2 = 1_827_362_000 + 1_234_519_000
+FWD_STATS_TRAFFIC_C2 = 503_297_000 + 5_941_000
+# DRAM bytes of one persistent backward launch at config 2 (same profile file; pair kernel).
+BWD_TRAFFIC_C2 = 1_885_633_000 + 1_120_405_000
 
 
 def load_peaks():
@@ -371,11 +371,14 @@ def main():
     # region, where the 1 kW power cap sets the clock: the sustained figure is the ceiling.
     k_peak = float(peaks.get("bf16_tflops_sustained", burst))
     sust = k_peak
+    # the library's choice of backward kernel (include/lmce.h: CTA pairs unless H < 256)
+    bwd_pair = H % 64 == 0 and H >= 256 and os.environ.get("LMCE_BWD_KERNEL") != "single"
     kernels = {
         "stats": {"name": "lmce_stats_kernel (fused logits GEMM + online softmax statistics)",
                   "ms": kern_ms[0], "alg_flops": 2.0 * n_tokens * H * v_local,
                   "exec_flops": 2.0 * n_tokens * H * v_local, "traffic": FWD_STATS_TRAFFIC_C2},
-        "backward": {"name": "lmce_bwd_kernel (persistent: recomputed logits -> G, dX and dW GEMMs)",
+        "backward": {"name": ("lmce_bwd_pair_kernel (persistent on CTA pairs" if bwd_pair else "lmce_bwd_kernel (persistent")
+                             + ": recomputed logits -> G, dX and dW GEMMs)",
                      "ms": kern_ms[1], "alg_flops": 4.0 * n_lab * H * v_local,
                      "exec_flops": 6.0 * n_lab * H * v_local, "traffic": BWD_TRAFFIC_C2},
     }
