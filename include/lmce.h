@@ -116,7 +116,7 @@ LMCE_API size_t lmce_bwd_workspace_bytes(int64_t n_tokens, int64_t hidden_dim, i
  * registers and contracts it into dX and dW (replaces ops.py:280-322 and
  * ops.py:333-339; dW is new). Only tokens with label != -100 are processed.
  * One persistent launch: on CTA pairs (tcgen05 cta_group::2) when hidden_dim
- * >= 256, else on single CTAs; LMCE_BWD_KERNEL=single forces the latter. */
+ * >= 256, else on single CTAs; LMCE_BWD_KERNEL=single forces the latter.
  *   lse        [n_tokens] fp32 from lmce_stats_finish (global over all shards)
  *   grad_loss  device fp32 scalar d(loss) (nullable: 1.0)
  *   denom      device fp32 scalar from lmce_stats_finish
