@@ -575,21 +575,25 @@ struct BwdLayout {
   int rows_pad, v_chunk, n_chunks, sync_ints;
 };
 
-// Default vocab chunk of the backward: G buffers of about 64 MiB. Few tokens per chunk
-// leave the dX chain and the per-chunk dependencies exposed, so small N prefers wide
-// chunks; large N prefers narrower ones to keep the chunk working set near L2.
-int64_t auto_v_chunk(int64_t rows_pad) {
-  int64_t vc = (64ll << 20) / (2 * rows_pad);
+// Default vocab chunk of the backward. Few tokens per chunk leave the dX chain and
+// the per-chunk dependencies exposed, so small N prefers wide chunks; large N prefers
+// narrower ones to bound the G buffers (three of N x v_chunk). Measured on one B200:
+// the pair kernel does best with G buffers of about 160 MiB and chunks of at most
+// 20480 rows, the one-CTA kernel with about 64 MiB and at most 32768 rows.
+int64_t auto_v_chunk(int64_t rows_pad, bool pair) {
+  const int64_t budget = pair ? (160ll << 20) : (64ll << 20);
+  int64_t vc = budget / (2 * rows_pad);
   vc = vc / 2048 * 2048;
   if (vc < 8192) vc = 8192;
-  if (vc > 32768) vc = 32768;
+  const int64_t vmax = pair ? 20480 : 32768;
+  if (vc > vmax) vc = vmax;
   return vc;
 }
 
 BwdLayout bwd_layout(int64_t n, int64_t h, int64_t v_local, int64_t v_chunk) {
   BwdLayout L{};
   const int64_t rows_pad = (n + BM - 1) / BM * BM;
-  int64_t vc = v_chunk <= 0 ? auto_v_chunk(rows_pad) : v_chunk;
+  int64_t vc = v_chunk <= 0 ? auto_v_chunk(rows_pad, use_pair_backward(h)) : v_chunk;
   vc = (vc + 255) / 256 * 256;
   const int64_t vmax = (v_local + 255) / 256 * 256;
   if (vc > vmax) vc = vmax;

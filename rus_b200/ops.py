@@ -265,6 +265,7 @@ def chunked_lm_head(hidden_states, shift_labels, weight_or_host_head, num_items_
     """Drop-in for ``solution.ops.chunked_lm_head`` (ops.py:342-349).
 
     ``v_chunk`` is the vocab chunk of the gradient pass; ``None`` (the default) lets the
-    library size it (gradient buffers of ~64 MiB), an explicit value is used as given."""
+    library size it (for the CTA-pair kernel gradient buffers of ~160 MiB, at most 20480
+    vocab rows); an explicit value is used as given."""
     return FusedChunkedLMHeadFn.apply(hidden_states, shift_labels, weight_or_host_head, num_items_in_batch,
                                       v_chunk)
