@@ -579,21 +579,27 @@ struct BwdLayout {
 // the per-chunk dependencies exposed, so small N prefers wide chunks; large N prefers
 // narrower ones to bound the G buffers (three of N x v_chunk). Measured on one B200:
 // the pair kernel does best with G buffers of about 160 MiB and chunks of at most
-// 20480 rows, the one-CTA kernel with about 64 MiB and at most 32768 rows.
-int64_t auto_v_chunk(int64_t rows_pad, bool pair) {
+// 20480 rows, the one-CTA kernel with about 64 MiB and at most 32768 rows. For few
+// tokens the chunk is also capped so that the G buffers stay at most half the size of
+// an [N, V] logits buffer: with the 256-row padding of the [rows, H] buffers the whole
+// workspace stays below [N, V] in the input dtype for every N >= 64.
+int64_t auto_v_chunk(int64_t n, int64_t rows_pad, int64_t v_local, bool pair) {
   const int64_t budget = pair ? (160ll << 20) : (64ll << 20);
   int64_t vc = budget / (2 * rows_pad);
   vc = vc / 2048 * 2048;
   if (vc < 8192) vc = 8192;
   const int64_t vmax = pair ? 20480 : 32768;
   if (vc > vmax) vc = vmax;
+  const int64_t g_rows = NUM_GBUF * ((n + 255) / 256 * 256);
+  const int64_t cap = (n * v_local / 2) / g_rows / 256 * 256;  // G bytes <= n * v_local bytes
+  if (vc > cap) vc = cap < 256 ? 256 : cap;
   return vc;
 }
 
 BwdLayout bwd_layout(int64_t n, int64_t h, int64_t v_local, int64_t v_chunk) {
   BwdLayout L{};
   const int64_t rows_pad = (n + BM - 1) / BM * BM;
-  int64_t vc = v_chunk <= 0 ? auto_v_chunk(rows_pad, use_pair_backward(h)) : v_chunk;
+  int64_t vc = v_chunk <= 0 ? auto_v_chunk(n, rows_pad, v_local, use_pair_backward(h)) : v_chunk;
   vc = (vc + 255) / 256 * 256;
   const int64_t vmax = (v_local + 255) / 256 * 256;
   if (vc > vmax) vc = vmax;

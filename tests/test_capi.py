@@ -48,6 +48,17 @@ def test_argument_validation_without_gpu():
     assert rc == _lib.LMCE_ERR_WORKSPACE
 
 
+def test_default_workspace_holds_no_logits_sized_buffer():
+    """The backward workspace with the library's default chunk (the op's largest transient
+    allocation) stays below an [N, V] buffer of the input dtype for every N >= 64 (below
+    that the 256-row padding of the gathered rows and the dX accumulator dominates)."""
+    lib = _lib.load()
+    for h, v in ((1536, 151936), (896, 151936), (4096, 128256), (128, 5000)):
+        for n in (64, 65, 100, 256, 880, 2048, 4096, 11600, 32768):
+            ws = lib.lmce_bwd_workspace_bytes(n, h, v, 0)
+            assert ws < n * v * 2, (n, h, v, ws)
+
+
 def test_workspace_sizes_are_bounded():
     lib = _lib.load()
     n, h, v = 2048, 1536, 151936
