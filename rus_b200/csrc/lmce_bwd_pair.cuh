@@ -570,7 +570,7 @@ __global__ void __launch_bounds__(P_THREADS, 1)
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
               const int j = 4 * j4 + u;
-              float pr = ex2_approx(fmaf(round_split<BF16>(v[j]), LOG2E, -lj[u]));
+              float pr = ex2_approx(fmaf(round_to_input<BF16>(v[j]), LOG2E, -lj[u]));
               if (hit) {  // warp-uniform
                 if (__shfl_sync(0xffffffffu, y_l, j) == vloc) pr -= 1.0f;
               }

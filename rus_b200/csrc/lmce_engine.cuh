@@ -90,20 +90,6 @@ __device__ __forceinline__ float round_to_input(float x) {
   }
 }
 
-// x rounded to the significand width of the input dtype (11 bits for fp16, 8 for
-// bf16) on the FP32 pipe: Veltkamp's split, hi = t - (t - x) with t = x * (2^s + 1),
-// s = 24 - width, keeps the leading bits of x rounded to nearest (T. J. Dekker, "A
-// floating-point technique for extending the available precision", 1971). Against
-// round_to_input it can differ only on exact ties and below the fp16 normal range,
-// and it never overflows to inf; the backward's G uses it, since two conversions per
-// logit would bound its epilogue by the conversion unit's rate.
-template <bool BF16>
-__device__ __forceinline__ float round_split(float x) {
-  constexpr float c = BF16 ? 65537.0f : 8193.0f;
-  const float t = __fmul_rn(x, c);
-  return __fsub_rn(t, __fsub_rn(t, x));
-}
-
 template <bool BF16>
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
   if constexpr (BF16) {
