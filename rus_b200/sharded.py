@@ -10,7 +10,7 @@ hidden states and labels are replicated. The two exchange steps:
 * backward: each rank contracts its shard's gradient tile into its local dW
   shard and an fp32 dX contribution, which is summed over the ranks. On GPUs
   that share an NVLink switch with multicast (NVLS) support, for dX of at least
-  64 MiB in fp32 (``LMCE_NVLS=1`` forces it, ``0`` disables it), the sum is
+  32 MiB in fp32 (``LMCE_NVLS=1`` forces it, ``0`` disables it), the sum is
   fused into the backward kernel (``lmce_backward_nvls``):
   as a row block's last-chunk dX tiles finish on every rank, each rank sums its
   slice of the block's columns over the GPUs through the switch
@@ -18,9 +18,10 @@ hidden states and labels are replicated. The two exchange steps:
   (``multimem.st``), while the last two chunks' dW tiles still compute. The
   buffers are torch symmetric memory, allocated once per shape. Otherwise one
   NCCL all-reduce sums the fp32 contributions after the kernel and
-  ``lmce_dx_finalize`` casts them to the input dtype. Measured on 8 B200s at the
-  config-2 shape: 3.58 ms per step fused against 3.90 with NCCL for 16384 tokens
-  (dX 100 MB); 0.84 against 0.80 ms for 2048 tokens (12.6 MB), hence the size rule.
+  ``lmce_dx_finalize`` casts them to the input dtype. Measured at the config-2 shape
+  (ms per step, fused / NCCL): 8 GPUs, 16384 tokens (dX 100 MB) 3.58 / 3.90; 4 GPUs,
+  8192 tokens (50 MB) 3.24 / 3.58; 2 GPUs, 4096 tokens (25 MB) 3.11 / 3.04; 2048
+  tokens (12.6 MB) on 4 and 8 GPUs 0.97 / 0.89 and 0.84 / 0.80; hence the size rule.
 
 The reference has no multi-GPU path (it pins one T4); this is the B200 build's
 addition for the same operator interface.
@@ -97,7 +98,7 @@ def _round_up(x: int, a: int) -> int:
     return (x + a - 1) // a * a
 
 
-NVLS_MIN_DX_BYTES = 64 << 20  # fp32 dX size from which the fused exchange beats NCCL's all-reduce
+NVLS_MIN_DX_BYTES = 32 << 20  # fp32 dX size from which the fused exchange beats NCCL's all-reduce
 
 
 def nvls_dx_exchange(n: int, h: int, dtype: torch.dtype, device: torch.device, group=None):
