@@ -178,6 +178,32 @@ LMCE_API int lmce_dx_copy_labelled(const void* src, const int64_t* labels, int64
 LMCE_API int lmce_dx_finalize(const float* d_hidden_f32, int64_t n_tokens, int64_t hidden_dim, int dtype,
                      void* d_hidden, void* stream);
 
+/* ------------------------------------------------ packing around the head */
+
+/* Packing before the head (replaces the label shift, keep mask and compaction of
+ * the patched Qwen2ForCausalLM.forward, ops.py:1107-1127). For labels [batch, seq]
+ * and an optional attention mask [batch, seq] (nonzero = attended; NULL = all),
+ * position t = b * seq + s has the shifted label labels[b, s + 1] (-100 for the
+ * last position) and is kept when it is attended or its shifted label is not
+ * -100; when no position is kept, position 0 of every row is. Kept positions are
+ * compacted in order into shift_labels[0, n) and valid_idx[0, n) (= t); *count
+ * (device int32) receives n and row_lengths[b] the kept positions of row b. With
+ * hidden ([batch * seq, hidden_dim], dtype) and hidden_packed (same size), the
+ * kept rows are gathered into hidden_packed[0, n). shift_labels and valid_idx
+ * need batch * seq entries. 1 <= batch * seq <= 2^22. */
+LMCE_API int lmce_pack_tokens(const int64_t* labels, const int64_t* attention_mask, int64_t batch, int64_t seq,
+                              int64_t* shift_labels, int64_t* valid_idx, int32_t* row_lengths, int32_t* count,
+                              const void* hidden, int64_t hidden_dim, int dtype, void* hidden_packed,
+                              void* stream);
+
+/* Scatter of the head's per-token outputs back to all `total` positions (replaces
+ * ops.py:1151-1164): position valid_idx[i] gets nll[i], entropy[i], argmax[i] for
+ * i < *count; every other position gets nll 0, argmax 0 and the mean entropy of
+ * the kept tokens (0 when none), computed on the device. */
+LMCE_API int lmce_scatter_token_outputs(const float* nll, const float* entropy, const int64_t* argmax,
+                                        const int64_t* valid_idx, const int32_t* count, int64_t total,
+                                        float* full_nll, float* full_entropy, int64_t* full_argmax, void* stream);
+
 /* ----------------------------------------------- no-allocation forward */
 
 /* Bytes of the library's fixed device scratch used by lmce_forward_noalloc. */

@@ -28,6 +28,11 @@ Contents
                     The per-token partial record (m, s, w, best, idx, zy) of a
                     vocab range and its merge — the statistics protocol the
                     vocab-sharded head gathers across GPUs.
+``pack_restatement`` / ``scatter_restatement``
+                    Plain-Python loops of the packing around the head: label
+                    shift, keep mask and compaction (solution/ops.py:1107-1127),
+                    and the scatter back with the mean-entropy filler
+                    (ops.py:1151-1164).
 
 Parity pin: tests/golden/ holds outputs of the reference's own ``chunked_lm_head``
 (run on CPU through Triton's interpreter, tests/golden/make_golden.py) on the
@@ -323,3 +328,31 @@ def make_config_inputs(cfg: str, seed: int = 0, device: str = "cpu", n_override:
             X[t] = (W[a].float() * (40.0 / W[a].float().norm())).to(dt)
     meta = dict(cfg=cfg, N=N, H=H, V=V, dtype=str(dt).replace("torch.", ""), lens=lens.tolist(), seed=seed)
     return X.to(device), labels.to(device), W.to(device), meta
+
+
+def pack_restatement(labels: torch.Tensor, mask: torch.Tensor | None):
+    """solution/ops.py:1107-1127 as loops: shift labels left (last position -100), keep a
+    position when attended or labelled, position 0 of every row when nothing is kept;
+    returns (shift labels of kept positions, their flat indices, kept count per row)."""
+    B, S = labels.shape
+    shift = [[IGNORE] * S for _ in range(B)]
+    for b in range(B):
+        for s in range(S - 1):
+            shift[b][s] = int(labels[b, s + 1])
+    keep = [[(mask is not None and bool(mask[b, s])) or (mask is None) or shift[b][s] != IGNORE for s in range(S)]
+            for b in range(B)]
+    if not any(any(r) for r in keep):
+        for b in range(B):
+            keep[b][0] = True
+    idx = [b * S + s for b in range(B) for s in range(S) if keep[b][s]]
+    return [shift[i // S][i % S] for i in idx], idx, [sum(r) for r in keep]
+
+
+def scatter_restatement(total: int, idx: list, nll: list, ent: list, arg: list):
+    """solution/ops.py:1151-1164 as loops: kept positions get their values, the others nll 0,
+    argmax 0 and the mean entropy of the kept tokens (0 when none)."""
+    mean = float(sum(ent)) / len(ent) if ent else 0.0
+    full_nll, full_ent, full_arg = [0.0] * total, [mean] * total, [0] * total
+    for i, t in enumerate(idx):
+        full_nll[t], full_ent[t], full_arg[t] = nll[i], ent[i], arg[i]
+    return full_nll, full_ent, full_arg

@@ -17,6 +17,7 @@
 #include "../../include/lmce.h"
 #include "lmce_bwd.cuh"
 #include "lmce_bwd_pair.cuh"
+#include "lmce_pack.cuh"
 
 using namespace lmce;
 
@@ -943,6 +944,54 @@ int lmce_dx_copy_labelled(const void* src, const int64_t* labels, int64_t n_toke
   if (blocks > d->sms * 8ll) blocks = d->sms * 8ll;
   dx_copy_labelled_kernel<<<static_cast<int>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint4*>(src), labels, vec, total, static_cast<uint4*>(d_hidden));
+  return launched();
+}
+
+int lmce_pack_tokens(const int64_t* labels, const int64_t* attention_mask, int64_t batch, int64_t seq,
+                     int64_t* shift_labels, int64_t* valid_idx, int32_t* row_lengths, int32_t* count,
+                     const void* hidden, int64_t hidden_dim, int dtype, void* hidden_packed, void* stream) {
+  if (!labels || !shift_labels || !valid_idx || !row_lengths || !count)
+    return fail(LMCE_ERR_INVALID_ARGUMENT, "null pointer");
+  if (batch <= 0 || seq <= 0 || batch * seq > (1ll << 22))
+    return fail(LMCE_ERR_INVALID_ARGUMENT, "bad batch/seq (1 <= B*S <= 2^22)");
+  if ((hidden == nullptr) != (hidden_packed == nullptr))
+    return fail(LMCE_ERR_INVALID_ARGUMENT, "hidden and hidden_packed go together");
+  if (hidden) {
+    if (hidden_dim <= 0 || hidden_dim % 8 != 0) return fail(LMCE_ERR_INVALID_ARGUMENT, "hidden_dim must be a multiple of 8");
+    if (dtype != LMCE_DTYPE_F16 && dtype != LMCE_DTYPE_BF16) return fail(LMCE_ERR_UNSUPPORTED, "dtype %d", dtype);
+    if (!aligned16(hidden) || !aligned16(hidden_packed)) return fail(LMCE_ERR_INVALID_ARGUMENT, "misaligned buffers");
+  }
+  DevInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  LMCE_CUDA(cudaMemsetAsync(row_lengths, 0, sizeof(int32_t) * batch, st));
+  pack_tokens_kernel<<<1, PACK_THREADS, 0, st>>>(labels, attention_mask, batch, seq, shift_labels, valid_idx,
+                                                 row_lengths, count);
+  if (int rc = launched()) return rc;
+  if (!hidden) return LMCE_OK;
+  const int vec = static_cast<int>(hidden_dim * 2 / 16);
+  long long blocks = (batch * seq * vec + 255) / 256;
+  if (blocks > d->sms * 8ll) blocks = d->sms * 8ll;
+  pack_rows_kernel<<<static_cast<int>(blocks), 256, 0, st>>>(static_cast<const uint4*>(hidden), vec, valid_idx,
+                                                             count, static_cast<uint4*>(hidden_packed));
+  return launched();
+}
+
+int lmce_scatter_token_outputs(const float* nll, const float* entropy, const int64_t* argmax,
+                               const int64_t* valid_idx, const int32_t* count, int64_t total, float* full_nll,
+                               float* full_entropy, int64_t* full_argmax, void* stream) {
+  if (!nll || !entropy || !argmax || !valid_idx || !count || !full_nll || !full_entropy || !full_argmax)
+    return fail(LMCE_ERR_INVALID_ARGUMENT, "null pointer");
+  if (total <= 0 || total > (1ll << 22)) return fail(LMCE_ERR_INVALID_ARGUMENT, "bad total (1 <= total <= 2^22)");
+  DevInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  fill_outputs_kernel<<<1, PACK_THREADS, 0, st>>>(entropy, count, total, full_nll, full_entropy, full_argmax);
+  if (int rc = launched()) return rc;
+  long long blocks = (total + 255) / 256;
+  if (blocks > d->sms * 4ll) blocks = d->sms * 4ll;
+  scatter_outputs_kernel<<<static_cast<int>(blocks), 256, 0, st>>>(nll, entropy, argmax, valid_idx, count, full_nll,
+                                                                   full_entropy, full_argmax);
   return launched();
 }
 

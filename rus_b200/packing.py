@@ -2,11 +2,13 @@
 scattering the head's per-token outputs back to [B, S] for the logits proxy.
 
 Mirrors the patched ``Qwen2ForCausalLM.forward`` of the reference
-(``solution/ops.py:1107-1127`` before the head, ``ops.py:1151-1184`` after it)
-without its host synchronisations: row lengths stay on the device (the
-reference's ``.tolist()`` at ops.py:1117 feeds its layer engine, which is not
-part of this path) and the entropy filler for dropped positions is the mean
-entropy computed on the device (the reference's ``.item()`` at ops.py:1161).
+(``solution/ops.py:1107-1127`` before the head, ``ops.py:1151-1184`` after it) with
+the library's own kernels (``lmce_pack_tokens``, ``lmce_scatter_token_outputs``): two
+launches each way, the kept count and the mean-entropy filler stay on the device, and
+the only host read is the kept count that sizes the packed tensors (the reference
+reads the row lengths with ``.tolist()`` at ops.py:1117, the mean entropy with
+``.item()`` at ops.py:1161, and ``torch.nonzero`` reads its count as well). CUDA
+tensors only: there is no CPU path.
 """
 from __future__ import annotations
 
@@ -14,7 +16,8 @@ from dataclasses import dataclass
 
 import torch
 
-from .ops import chunked_lm_head
+from . import _lib
+from .ops import _DTYPES, _stream, chunked_lm_head
 from .proxy import ChunkedLogitsProxy
 
 IGNORE = -100
@@ -27,36 +30,65 @@ class PackedBatch:
     row_lengths: torch.Tensor    # [B] int32 kept positions per row (device)
     batch: int
     seq: int
+    count: torch.Tensor | None = None          # [1] int32 N on the device
+    hidden_packed: torch.Tensor | None = None  # [N, H] kept rows of the hidden states, when asked for
 
 
-def shift_and_pack(labels: torch.Tensor, attention_mask: torch.Tensor | None = None) -> PackedBatch:
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def shift_and_pack(labels: torch.Tensor, attention_mask: torch.Tensor | None = None,
+                   hidden: torch.Tensor | None = None) -> PackedBatch:
     """ops.py:1107-1127: shift labels left by one (last position -100), keep positions that are
-    attended or carry a label (at least one token per batch), and pack them."""
+    attended or carry a label (position 0 of every row when none is kept), and pack them; with
+    ``hidden`` ([B, S, H] fp16/bf16) the kept rows are gathered as well."""
+    if labels.device.type != "cuda":
+        raise RuntimeError("shift_and_pack runs on CUDA tensors only (no CPU path)")
     B, S = labels.shape
     dev = labels.device
-    if attention_mask is None:
-        attention_mask = torch.ones((B, S), dtype=torch.long, device=dev)
-    shift = torch.full((B, S), IGNORE, dtype=torch.int64, device=dev)
-    if S > 1:
-        shift[:, :-1] = labels[:, 1:].to(torch.int64)
-    keep = attention_mask.bool() | (shift != IGNORE)
-    # at least one token per batch (ops.py:1113-1115), without a host round trip
-    none_kept = ~keep.any()
-    keep[:, 0] |= none_kept
-    valid_idx = torch.nonzero(keep.reshape(-1), as_tuple=False).squeeze(-1)
-    return PackedBatch(shift_labels=shift.reshape(-1).index_select(0, valid_idx), valid_idx=valid_idx,
-                       row_lengths=keep.sum(dim=-1, dtype=torch.int32), batch=B, seq=S)
+    total = B * S
+    lab = labels.to(torch.int64).contiguous()
+    mask = None if attention_mask is None else attention_mask.to(device=dev, dtype=torch.int64).contiguous()
+    shift = torch.empty(total, dtype=torch.int64, device=dev)
+    idx = torch.empty(total, dtype=torch.int64, device=dev)
+    row_lengths = torch.empty(B, dtype=torch.int32, device=dev)
+    count = torch.empty(1, dtype=torch.int32, device=dev)
+    h2d, hp, hdim, dt = None, None, 0, 0
+    if hidden is not None:
+        hdim = hidden.shape[-1]
+        h2d = hidden.reshape(total, hdim).contiguous()
+        hp = torch.empty_like(h2d)
+        dt = _DTYPES[h2d.dtype]
+    with torch.cuda.device(dev):
+        _lib.call("lmce_pack_tokens", lab.data_ptr(), _ptr(mask), B, S, shift.data_ptr(), idx.data_ptr(),
+                  row_lengths.data_ptr(), count.data_ptr(), _ptr(h2d), hdim, dt, _ptr(hp), _stream(dev))
+    n = int(count.item())  # the one host read: sizes the packed tensors
+    return PackedBatch(shift_labels=shift[:n], valid_idx=idx[:n], row_lengths=row_lengths, batch=B, seq=S,
+                       count=count, hidden_packed=hp[:n] if hp is not None else None)
 
 
 def scatter_head_outputs(packed: PackedBatch, nll: torch.Tensor, entropy: torch.Tensor, argmax: torch.Tensor):
     """ops.py:1151-1164: per-token outputs back to [B, S]; dropped positions get nll 0,
-    argmax 0 and the mean entropy of the kept tokens."""
+    argmax 0 and the mean entropy of the kept tokens (computed on the device)."""
     B, S = packed.batch, packed.seq
     dev = nll.device
-    full_nll = torch.zeros(B * S, dtype=torch.float32, device=dev).index_copy_(0, packed.valid_idx, nll)
-    full_arg = torch.zeros(B * S, dtype=torch.int64, device=dev).index_copy_(0, packed.valid_idx, argmax)
-    mean_ent = entropy.mean() if entropy.numel() > 0 else torch.zeros((), dtype=torch.float32, device=dev)
-    full_ent = mean_ent.expand(B * S).clone().index_copy_(0, packed.valid_idx, entropy)
+    if dev.type != "cuda":
+        raise RuntimeError("scatter_head_outputs runs on CUDA tensors only (no CPU path)")
+    count = packed.count
+    if count is None:
+        count = torch.tensor([packed.valid_idx.numel()], dtype=torch.int32, device=dev)
+    full_nll = torch.empty(B * S, dtype=torch.float32, device=dev)
+    full_ent = torch.empty(B * S, dtype=torch.float32, device=dev)
+    full_arg = torch.empty(B * S, dtype=torch.int64, device=dev)
+    nll_c = nll.to(torch.float32).contiguous()
+    ent_c = entropy.to(torch.float32).contiguous()
+    arg_c = argmax.to(torch.int64).contiguous()
+    idx = packed.valid_idx.contiguous()
+    with torch.cuda.device(dev):
+        _lib.call("lmce_scatter_token_outputs", nll_c.data_ptr(), ent_c.data_ptr(), arg_c.data_ptr(), idx.data_ptr(),
+                  count.data_ptr(), B * S, full_nll.data_ptr(), full_ent.data_ptr(), full_arg.data_ptr(),
+                  _stream(dev))
     return full_nll.view(B, S), full_ent.view(B, S), full_arg.view(B, S)
 
 

@@ -1,4 +1,4 @@
-"""CPU: ChunkedLogitsProxy and the packing around the head (host logic).
+"""CPU: ChunkedLogitsProxy, and the oracle's restatement of the packing around the head.
 
 The proxy is fed the oracle's per-token statistics of the reference's known-answer
 case (solution/test_kernels.py:189-241) and must answer the expressions TRL and
@@ -13,7 +13,7 @@ import torch
 import torch.nn.functional as F
 
 from oracle import lmce_oracle as orc
-from rus_b200.packing import scatter_head_outputs, shift_and_pack
+from rus_b200.packing import shift_and_pack
 from rus_b200.proxy import ChunkedLogitsProxy, fast_entropy_from_logits
 
 
@@ -95,53 +95,22 @@ def test_layout_noops_keep_identity(ref_case):
     assert p.contiguous() is p and p.detach() is p and p.clone() is p
 
 
-def _pack_loop(labels, mask):
-    """Plain-Python restatement of ops.py:1107-1127 for checking."""
-    B, S = labels.shape
-    shift = [[-100] * S for _ in range(B)]
-    for b in range(B):
-        for s in range(S - 1):
-            shift[b][s] = int(labels[b, s + 1])
-    keep = [[bool(mask[b, s]) or shift[b][s] != -100 for s in range(S)] for b in range(B)]
-    if not any(any(r) for r in keep):
-        for b in range(B):
-            keep[b][0] = True
-    idx = [b * S + s for b in range(B) for s in range(S) if keep[b][s]]
-    return [shift[i // S][i % S] for i in idx], idx, [sum(r) for r in keep]
-
-
-@pytest.mark.parametrize("pattern", ["padded", "all_padded_no_labels", "full"])
-def test_shift_and_pack_matches_reference_logic(pattern):
-    g = torch.Generator().manual_seed(4)
-    B, S, V = 3, 17, 50
-    labels = torch.randint(0, V, (B, S), generator=g)
-    mask = torch.ones(B, S, dtype=torch.long)
-    if pattern == "padded":
-        mask[0, 12:] = 0
-        labels[0, 12:] = -100
-        mask[2, 5:] = 0
-        labels[2, 3:] = -100
-    elif pattern == "all_padded_no_labels":
-        mask[:] = 0
-        labels[:] = -100
-    packed = shift_and_pack(labels, mask)
-    lab, idx, lens = _pack_loop(labels, mask)
-    assert packed.shift_labels.tolist() == lab
-    assert packed.valid_idx.tolist() == idx
-    assert packed.row_lengths.tolist() == lens
-
-
-def test_scatter_fills_dropped_positions_with_mean_entropy():
+def test_pack_restatement_known_case():
+    """The oracle's loop restatement of ops.py:1107-1127 on a hand-checked case."""
     labels = torch.tensor([[5, 6, 7, -100], [1, 2, -100, -100]])
     mask = torch.tensor([[1, 1, 1, 0], [1, 1, 0, 0]])
-    packed = shift_and_pack(labels, mask)
-    n = packed.valid_idx.numel()
-    nll = torch.arange(1, n + 1, dtype=torch.float32)
-    ent = torch.linspace(0.5, 2.0, n)
-    arg = torch.arange(10, 10 + n)
-    full_nll, full_ent, full_arg = scatter_head_outputs(packed, nll, ent, arg)
-    kept = torch.zeros(8, dtype=torch.bool)
-    kept[packed.valid_idx] = True
-    assert torch.equal(full_nll.view(-1)[kept], nll) and (full_nll.view(-1)[~kept] == 0).all()
-    assert torch.allclose(full_ent.view(-1)[~kept], ent.mean().expand(int((~kept).sum())))
-    assert torch.equal(full_arg.view(-1)[kept], arg)
+    lab, idx, lens = orc.pack_restatement(labels, mask)
+    # row 0: shifted 6, 7, -100, -100; attended 0..2 -> keep 0, 1, 2
+    # row 1: shifted 2, -100, -100, -100; attended 0, 1 -> keep 4, 5
+    assert idx == [0, 1, 2, 4, 5] and lab == [6, 7, -100, 2, -100] and lens == [3, 2]
+    lab, idx, lens = orc.pack_restatement(torch.full((2, 3), -100), torch.zeros(2, 3, dtype=torch.long))
+    assert idx == [0, 3] and lab == [-100, -100] and lens == [1, 1]
+    full = orc.scatter_restatement(6, [1, 4], [1.0, 2.0], [0.5, 1.5], [7, 8])
+    assert full == ([0.0, 1.0, 0.0, 0.0, 2.0, 0.0], [1.0, 0.5, 1.0, 1.0, 1.5, 1.0], [0, 7, 0, 0, 8, 0])
+
+
+def test_packing_refuses_cpu_tensors():
+    """The product path has no CPU fallback."""
+    labels = torch.tensor([[5, 6, 7, -100]])
+    with pytest.raises(RuntimeError, match="CUDA"):
+        shift_and_pack(labels)
