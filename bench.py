@@ -46,10 +46,11 @@ CONFIGS = {
     "c4": (8, 4096, 4096, 128256, torch.bfloat16, 0.0),
 }
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
-# DRAM bytes (read + write) of one forward-statistics launch at config 2, from
-# one `ncu --set full` capture (profiles/lmce_head_c2_fwd_bwd.md).
+# DRAM bytes (read + write) of one forward-statistics launch at config 2, from one
+# `ncu --set full` capture (dram__bytes_read.sum + dram__bytes_write.sum) of the second
+# step of two config-2 steps run through chunked_lm_head.
 FWD_STATS_TRAFFIC_C2 = 503_297_000 + 5_941_000
-# DRAM bytes of one persistent backward launch at config 2 (same profile file; pair kernel).
+# DRAM bytes of one persistent backward launch at config 2 (same capture; pair kernel).
 BWD_TRAFFIC_C2 = 1_885_633_000 + 1_120_405_000
 
 
