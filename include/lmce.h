@@ -204,6 +204,32 @@ LMCE_API int lmce_scatter_token_outputs(const float* nll, const float* entropy, 
                                         const int64_t* valid_idx, const int32_t* count, int64_t total,
                                         float* full_nll, float* full_entropy, int64_t* full_argmax, void* stream);
 
+/* ------------------------------------------------ tied input embedding */
+
+/* Bytes of the workspace lmce_embedding_grad_add needs. */
+LMCE_API size_t lmce_embedding_grad_workspace_bytes(int64_t n_tokens, int64_t vocab_local);
+
+/* Gradient of a tied input embedding added into the head's dW, so the weight's two
+ * contributions share one buffer instead of two [V, H] tensors that autograd adds
+ * (the reference's forward lookup is HostHead.embed, hostload.py:381-386; it has no
+ * weight gradient). For every position i whose token id lies in
+ * [vocab_offset, vocab_offset + vocab_local):
+ *   d_weight[id - vocab_offset, :] += d_embed[i, :]
+ * summed per id in fp64 with the existing value and rounded once to dtype
+ * (deterministic: independent of the order of positions).
+ *   d_embed    [n_tokens, hidden_dim] dtype, gradient of the lookup's output
+ *   token_ids  [n_tokens] int64
+ *   d_weight   [vocab_local, hidden_dim] dtype, updated in place */
+LMCE_API int lmce_embedding_grad_add(const void* d_embed, const int64_t* token_ids, int64_t n_tokens,
+                                     int64_t hidden_dim, int64_t vocab_local, int64_t vocab_offset, int dtype,
+                                     void* d_weight, void* workspace, size_t workspace_bytes, void* stream);
+
+/* out[i, :] = weight[token_ids[i] - vocab_offset, :] (zero rows for ids outside the
+ * shard); [n_tokens, hidden_dim] of a 16-bit dtype. */
+LMCE_API int lmce_embedding_lookup(const void* weight, const int64_t* token_ids, int64_t n_tokens,
+                                   int64_t hidden_dim, int64_t vocab_local, int64_t vocab_offset, void* out,
+                                   void* stream);
+
 /* ----------------------------------------------- no-allocation forward */
 
 /* Bytes of the library's fixed device scratch used by lmce_forward_noalloc. */

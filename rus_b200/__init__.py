@@ -7,5 +7,6 @@ and its backward produces dX and dW from hand-written tcgen05/TMA kernels
 (``liblmce.so``, C ABI in include/lmce.h).
 """
 from .ops import V_CHUNK_DEFAULT, FusedChunkedLMHeadFn, chunked_lm_head
+from .tied import TiedGradSlot, tied_embedding
 
-__all__ = ["V_CHUNK_DEFAULT", "FusedChunkedLMHeadFn", "chunked_lm_head"]
+__all__ = ["V_CHUNK_DEFAULT", "FusedChunkedLMHeadFn", "chunked_lm_head", "TiedGradSlot", "tied_embedding"]

@@ -18,6 +18,7 @@
 #include "lmce_bwd.cuh"
 #include "lmce_bwd_pair.cuh"
 #include "lmce_pack.cuh"
+#include "lmce_embed.cuh"
 
 using namespace lmce;
 
@@ -992,6 +993,75 @@ int lmce_scatter_token_outputs(const float* nll, const float* entropy, const int
   if (blocks > d->sms * 4ll) blocks = d->sms * 4ll;
   scatter_outputs_kernel<<<static_cast<int>(blocks), 256, 0, st>>>(nll, entropy, argmax, valid_idx, count, full_nll,
                                                                    full_entropy, full_argmax);
+  return launched();
+}
+
+size_t lmce_embedding_grad_workspace_bytes(int64_t n_tokens, int64_t vocab_local) {
+  if (n_tokens <= 0 || vocab_local <= 0) return 0;
+  return align_up(sizeof(int) * (4 * static_cast<size_t>(vocab_local) + 1), 256) +
+         align_up(sizeof(int) * static_cast<size_t>(n_tokens), 256);
+}
+
+int lmce_embedding_grad_add(const void* d_embed, const int64_t* token_ids, int64_t n_tokens, int64_t hidden_dim,
+                            int64_t vocab_local, int64_t vocab_offset, int dtype, void* d_weight, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  if (!d_embed || !token_ids || !d_weight || !workspace) return fail(LMCE_ERR_INVALID_ARGUMENT, "null pointer");
+  if (n_tokens <= 0 || n_tokens > (1ll << 30) || vocab_local <= 0 || vocab_local > (1ll << 30) || vocab_offset < 0)
+    return fail(LMCE_ERR_INVALID_ARGUMENT, "bad sizes");
+  if (hidden_dim <= 0 || hidden_dim % 8 != 0) return fail(LMCE_ERR_INVALID_ARGUMENT, "hidden_dim must be a multiple of 8");
+  if (dtype != LMCE_DTYPE_F16 && dtype != LMCE_DTYPE_BF16) return fail(LMCE_ERR_UNSUPPORTED, "dtype %d", dtype);
+  if (!aligned16(d_embed) || !aligned16(d_weight) || !aligned16(workspace))
+    return fail(LMCE_ERR_INVALID_ARGUMENT, "misaligned buffers");
+  if (workspace_bytes < lmce_embedding_grad_workspace_bytes(n_tokens, vocab_local))
+    return fail(LMCE_ERR_WORKSPACE, "workspace %zu bytes < required %zu", workspace_bytes,
+                lmce_embedding_grad_workspace_bytes(n_tokens, vocab_local));
+  DevInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int vl = static_cast<int>(vocab_local), h = static_cast<int>(hidden_dim);
+  int* counts = static_cast<int*>(workspace);
+  int* offsets = counts + vl;
+  int* cursor = offsets + vl;
+  int* used = cursor + vl;
+  int* n_used = used + vl;
+  int* order = reinterpret_cast<int*>(static_cast<char*>(workspace) +
+                                      align_up(sizeof(int) * (4 * static_cast<size_t>(vl) + 1), 256));
+  LMCE_CUDA(cudaMemsetAsync(counts, 0, sizeof(int) * vl, st));
+  long long blocks = (n_tokens + 255) / 256;
+  if (blocks > d->sms * 4ll) blocks = d->sms * 4ll;
+  emb_hist_kernel<<<static_cast<int>(blocks), 256, 0, st>>>(token_ids, n_tokens, vocab_offset, vl, counts);
+  if (int rc = launched()) return rc;
+  emb_scan_kernel<<<1, PACK_THREADS, 0, st>>>(counts, vl, offsets, cursor, used, n_used);
+  if (int rc = launched()) return rc;
+  emb_scatter_kernel<<<static_cast<int>(blocks), 256, 0, st>>>(token_ids, n_tokens, vocab_offset, vl, cursor, order);
+  if (int rc = launched()) return rc;
+  const long long max_used = n_tokens < vocab_local ? n_tokens : vocab_local;  // ids that can occur
+  const long long tasks = max_used * ((h + EMB_COLS - 1) / EMB_COLS);
+  const long long ablocks = (tasks * 32 + 255) / 256;
+  if (ablocks > (1ll << 31) - 1) return fail(LMCE_ERR_UNSUPPORTED, "too many rows");
+  if (dtype == LMCE_DTYPE_BF16)
+    emb_accumulate_kernel<true><<<static_cast<int>(ablocks), 256, 0, st>>>(
+        static_cast<const uint4*>(d_embed), h, used, n_used, counts, offsets, order, static_cast<uint4*>(d_weight));
+  else
+    emb_accumulate_kernel<false><<<static_cast<int>(ablocks), 256, 0, st>>>(
+        static_cast<const uint4*>(d_embed), h, used, n_used, counts, offsets, order, static_cast<uint4*>(d_weight));
+  return launched();
+}
+
+int lmce_embedding_lookup(const void* weight, const int64_t* token_ids, int64_t n_tokens, int64_t hidden_dim,
+                          int64_t vocab_local, int64_t vocab_offset, void* out, void* stream) {
+  if (!weight || !token_ids || !out) return fail(LMCE_ERR_INVALID_ARGUMENT, "null pointer");
+  if (n_tokens <= 0 || vocab_local <= 0 || vocab_offset < 0) return fail(LMCE_ERR_INVALID_ARGUMENT, "bad sizes");
+  if (hidden_dim <= 0 || hidden_dim % 8 != 0) return fail(LMCE_ERR_INVALID_ARGUMENT, "hidden_dim must be a multiple of 8");
+  if (!aligned16(weight) || !aligned16(out)) return fail(LMCE_ERR_INVALID_ARGUMENT, "misaligned buffers");
+  DevInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+  const int vec = static_cast<int>(hidden_dim * 2 / 16);
+  long long blocks = (n_tokens * vec + 255) / 256;
+  if (blocks > d->sms * 8ll) blocks = d->sms * 8ll;
+  emb_lookup_kernel<<<static_cast<int>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(weight), token_ids, n_tokens, vec, vocab_offset, static_cast<int>(vocab_local),
+      static_cast<uint4*>(out));
   return launched();
 }
 

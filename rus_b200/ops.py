@@ -214,7 +214,8 @@ class FusedChunkedLMHeadFn(torch.autograd.Function):
     ``hidden_states @ weight.T`` without materialising the [N, V] logits."""
 
     @staticmethod
-    def forward(ctx, hidden_states, shift_labels, weight_or_host_head, num_items_in_batch=None, v_chunk=None):
+    def forward(ctx, hidden_states, shift_labels, weight_or_host_head, num_items_in_batch=None, v_chunk=None,
+                tied_slot=None):
         weight = weight_or_host_head
         _check_inputs(hidden_states, shift_labels, weight)
         h2d = hidden_states.contiguous().view(-1, hidden_states.shape[-1])
@@ -239,6 +240,7 @@ class FusedChunkedLMHeadFn(torch.autograd.Function):
         ctx.save_for_backward(h2d, w, labels, lse, denom)
         ctx.orig_shape = hidden_states.shape
         ctx.v_chunk = int(v_chunk) if v_chunk else 0  # 0: the library's default chunk
+        ctx.tied_slot = tied_slot
         ctx.mark_non_differentiable(nll, ent, arg)
         return loss, nll, ent, arg
 
@@ -248,24 +250,30 @@ class FusedChunkedLMHeadFn(torch.autograd.Function):
         want_dx = ctx.needs_input_grad[0]
         want_dw = ctx.needs_input_grad[2]
         if not (want_dx or want_dw):
-            return None, None, None, None, None
+            return None, None, None, None, None, None
         if h2d.shape[0] == 0:
             dx = torch.zeros(ctx.orig_shape, dtype=h2d.dtype, device=h2d.device) if want_dx else None
             dw = torch.zeros_like(w) if want_dw else None
-            return dx, None, dw, None, None
-        with torch.cuda.device(h2d.device):
-            dx, dw = head_backward(h2d, w, labels, lse, grad_loss, denom, want_dx, want_dw, ctx.v_chunk)
-        if dx is not None:
-            dx = dx.view(ctx.orig_shape)
-        return dx, None, dw, None, None
+        else:
+            with torch.cuda.device(h2d.device):
+                dx, dw = head_backward(h2d, w, labels, lse, grad_loss, denom, want_dx, want_dw, ctx.v_chunk)
+            if dx is not None:
+                dx = dx.view(ctx.orig_shape)
+        if dw is not None and ctx.tied_slot is not None:
+            # tied input embedding: its backward adds into this buffer and returns the sum
+            ctx.tied_slot.dw = dw
+            dw = None
+        return dx, None, dw, None, None, None
 
 
 def chunked_lm_head(hidden_states, shift_labels, weight_or_host_head, num_items_in_batch=None,
-                    v_chunk: int | None = None):
+                    v_chunk: int | None = None, tied_slot=None):
     """Drop-in for ``solution.ops.chunked_lm_head`` (ops.py:342-349).
 
     ``v_chunk`` is the vocab chunk of the gradient pass; ``None`` (the default) lets the
     library size it (for the CTA-pair kernel gradient buffers of ~160 MiB, at most 20480
-    vocab rows); an explicit value is used as given."""
+    vocab rows); an explicit value is used as given. ``tied_slot`` (a
+    ``rus_b200.tied.TiedGradSlot`` shared with ``tied_embedding``) hands dW to the tied
+    input embedding's backward, which adds its own gradient into the same buffer."""
     return FusedChunkedLMHeadFn.apply(hidden_states, shift_labels, weight_or_host_head, num_items_in_batch,
-                                      v_chunk)
+                                      v_chunk, tied_slot)
