@@ -204,6 +204,28 @@ LMCE_API int lmce_scatter_token_outputs(const float* nll, const float* entropy, 
                                         const int64_t* valid_idx, const int32_t* count, int64_t total,
                                         float* full_nll, float* full_entropy, int64_t* full_argmax, void* stream);
 
+/* ------------------------------------------------ final RMSNorm + packing */
+
+/* Final RMSNorm fused with the packing gather (the reference normalises every row
+ * with rms_norm_fwd, ops.py:824 / kernels.py:124-164, before packing): for i < n,
+ * n = *count when count is given (device, from lmce_pack_tokens; n_rows is then an
+ * upper bound) else n_rows, with r = row_idx[i] (NULL: r = i):
+ *   rstd_out[i] = rsqrt(mean(hidden[r, :]^2) + eps)            (fp32)
+ *   x_out[i, :] = dtype(dtype(hidden[r, :] * rstd_out[i]) * weight)
+ * hidden [rows, hidden_dim] and weight [hidden_dim] in dtype; x_out [n_rows, hidden_dim]. */
+LMCE_API int lmce_rmsnorm_pack(const void* hidden, const void* weight, float eps, const int64_t* row_idx,
+                               const int32_t* count, int64_t n_rows, int64_t hidden_dim, int dtype, void* x_out,
+                               float* rstd_out, void* stream);
+
+/* Its backward fused with the scatter (ops.py:850 / kernels.py:167-190): for the same
+ * rows, with x_hat = hidden[r] * rstd[i], wdy = weight * d_x[i]:
+ *   d_hidden[r, :] = (wdy - x_hat * mean(x_hat * wdy)) * rstd[i]
+ * Rows of d_hidden that no i maps to are left unchanged (zero them first). The
+ * weight's gradient is not computed (the reference keeps the norm weight frozen). */
+LMCE_API int lmce_rmsnorm_backward(const void* d_x, const void* hidden, const void* weight, const float* rstd,
+                                   const int64_t* row_idx, const int32_t* count, int64_t n_rows, int64_t hidden_dim,
+                                   int dtype, void* d_hidden, void* stream);
+
 /* ------------------------------------------------ tied input embedding */
 
 /* Bytes of the workspace lmce_embedding_grad_add needs. */

@@ -28,6 +28,11 @@ Contents
                     The per-token partial record (m, s, w, best, idx, zy) of a
                     vocab range and its merge — the statistics protocol the
                     vocab-sharded head gathers across GPUs.
+``rms_norm_ref``    The reference's final RMSNorm as differentiable torch ops with its
+                    casting order (solution/kernels.py:124-164): rstd in fp32, the
+                    normalised row rounded to the input dtype, times the weight,
+                    rounded again; ``rms_norm_bwd_ref`` its backward formula
+                    (kernels.py:167-190).
 ``pack_restatement`` / ``scatter_restatement``
                     Plain-Python loops of the packing around the head: label
                     shift, keep mask and compaction (solution/ops.py:1107-1127),
@@ -356,3 +361,20 @@ def scatter_restatement(total: int, idx: list, nll: list, ent: list, arg: list):
     for i, t in enumerate(idx):
         full_nll[t], full_ent[t], full_arg[t] = nll[i], ent[i], arg[i]
     return full_nll, full_ent, full_arg
+
+
+def rms_norm_ref(h: torch.Tensor, w: torch.Tensor, eps: float = 1e-6):
+    """solution/kernels.py:124-164 without residual: (out, rstd); differentiable in h."""
+    hf = h.float()
+    rstd = torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + eps)
+    normed = (hf * rstd).to(h.dtype)
+    out = (normed.float() * w.float()).to(h.dtype)
+    return out, rstd.squeeze(-1)
+
+
+def rms_norm_bwd_ref(dy: torch.Tensor, h: torch.Tensor, w: torch.Tensor, rstd: torch.Tensor) -> torch.Tensor:
+    """solution/kernels.py:167-190 without residual: dh = (w dy - x_hat mean(x_hat w dy)) rstd."""
+    x_hat = h.float() * rstd[..., None]
+    wdy = w.float() * dy.float()
+    c1 = (x_hat * wdy).mean(-1, keepdim=True)
+    return ((wdy - x_hat * c1) * rstd[..., None]).to(h.dtype)

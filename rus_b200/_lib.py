@@ -87,6 +87,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "lmce_embedding_grad_workspace_bytes": (ctypes.c_size_t, [_i64, _i64]),
     "lmce_embedding_grad_add": (_int, [_vp, _vp, _i64, _i64, _i64, _i64, _int, _vp, _vp, ctypes.c_size_t, _vp]),
     "lmce_embedding_lookup": (_int, [_vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp]),
+    "lmce_rmsnorm_pack": (_int, [_vp, _vp, ctypes.c_float, _vp, _vp, _i64, _i64, _int, _vp, _vp, _vp]),
+    "lmce_rmsnorm_backward": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _int, _vp, _vp]),
     "lmce_dx_finalize": (_int, [_vp, _i64, _i64, _int, _vp, _vp]),
     "lmce_selftest_wait_timeout": (_int, [ctypes.c_uint64, _vp]),
     "lmce_launch_count": (ctypes.c_uint64, []),

@@ -19,6 +19,7 @@
 #include "lmce_bwd_pair.cuh"
 #include "lmce_pack.cuh"
 #include "lmce_embed.cuh"
+#include "lmce_rmsnorm.cuh"
 
 using namespace lmce;
 
@@ -1062,6 +1063,59 @@ int lmce_embedding_lookup(const void* weight, const int64_t* token_ids, int64_t 
   emb_lookup_kernel<<<static_cast<int>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint4*>(weight), token_ids, n_tokens, vec, vocab_offset, static_cast<int>(vocab_local),
       static_cast<uint4*>(out));
+  return launched();
+}
+
+int lmce_rmsnorm_pack(const void* hidden, const void* weight, float eps, const int64_t* row_idx,
+                      const int32_t* count, int64_t n_rows, int64_t hidden_dim, int dtype, void* x_out,
+                      float* rstd_out, void* stream) {
+  if (!hidden || !weight || !x_out || !rstd_out) return fail(LMCE_ERR_INVALID_ARGUMENT, "null pointer");
+  if (n_rows <= 0 || n_rows > (1ll << 30)) return fail(LMCE_ERR_INVALID_ARGUMENT, "bad n_rows");
+  if (hidden_dim <= 0 || hidden_dim % 8 != 0) return fail(LMCE_ERR_INVALID_ARGUMENT, "hidden_dim must be a multiple of 8");
+  if (dtype != LMCE_DTYPE_F16 && dtype != LMCE_DTYPE_BF16) return fail(LMCE_ERR_UNSUPPORTED, "dtype %d", dtype);
+  if (!aligned16(hidden) || !aligned16(weight) || !aligned16(x_out)) return fail(LMCE_ERR_INVALID_ARGUMENT, "misaligned buffers");
+  DevInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+  const int vec = static_cast<int>(hidden_dim / 8);
+  long long blocks = (n_rows * 32 + 255) / 256;
+  if (blocks > d->sms * 16ll) blocks = d->sms * 16ll;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const float inv = 1.0f / static_cast<float>(hidden_dim);
+  if (dtype == LMCE_DTYPE_BF16)
+    rmsnorm_pack_kernel<true><<<static_cast<int>(blocks), 256, 0, st>>>(
+        static_cast<const uint4*>(hidden), static_cast<const uint4*>(weight), row_idx, count, n_rows, vec, inv, eps,
+        static_cast<uint4*>(x_out), rstd_out);
+  else
+    rmsnorm_pack_kernel<false><<<static_cast<int>(blocks), 256, 0, st>>>(
+        static_cast<const uint4*>(hidden), static_cast<const uint4*>(weight), row_idx, count, n_rows, vec, inv, eps,
+        static_cast<uint4*>(x_out), rstd_out);
+  return launched();
+}
+
+int lmce_rmsnorm_backward(const void* d_x, const void* hidden, const void* weight, const float* rstd,
+                          const int64_t* row_idx, const int32_t* count, int64_t n_rows, int64_t hidden_dim, int dtype,
+                          void* d_hidden, void* stream) {
+  if (!d_x || !hidden || !weight || !rstd || !d_hidden) return fail(LMCE_ERR_INVALID_ARGUMENT, "null pointer");
+  if (n_rows <= 0 || n_rows > (1ll << 30)) return fail(LMCE_ERR_INVALID_ARGUMENT, "bad n_rows");
+  if (hidden_dim <= 0 || hidden_dim % 8 != 0) return fail(LMCE_ERR_INVALID_ARGUMENT, "hidden_dim must be a multiple of 8");
+  if (dtype != LMCE_DTYPE_F16 && dtype != LMCE_DTYPE_BF16) return fail(LMCE_ERR_UNSUPPORTED, "dtype %d", dtype);
+  if (!aligned16(d_x) || !aligned16(hidden) || !aligned16(weight) || !aligned16(d_hidden))
+    return fail(LMCE_ERR_INVALID_ARGUMENT, "misaligned buffers");
+  DevInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+  const int vec = static_cast<int>(hidden_dim / 8);
+  long long blocks = (n_rows * 32 + 255) / 256;
+  if (blocks > d->sms * 16ll) blocks = d->sms * 16ll;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const float inv = 1.0f / static_cast<float>(hidden_dim);
+  if (dtype == LMCE_DTYPE_BF16)
+    rmsnorm_backward_kernel<true><<<static_cast<int>(blocks), 256, 0, st>>>(
+        static_cast<const uint4*>(d_x), static_cast<const uint4*>(hidden), static_cast<const uint4*>(weight), rstd,
+        row_idx, count, n_rows, vec, inv, static_cast<uint4*>(d_hidden));
+  else
+    rmsnorm_backward_kernel<false><<<static_cast<int>(blocks), 256, 0, st>>>(
+        static_cast<const uint4*>(d_x), static_cast<const uint4*>(hidden), static_cast<const uint4*>(weight), rstd,
+        row_idx, count, n_rows, vec, inv, static_cast<uint4*>(d_hidden));
   return launched();
 }
 

@@ -92,6 +92,52 @@ def scatter_head_outputs(packed: PackedBatch, nll: torch.Tensor, entropy: torch.
     return full_nll.view(B, S), full_ent.view(B, S), full_arg.view(B, S)
 
 
+class RMSNormPackFn(torch.autograd.Function):
+    """Final RMSNorm of the kept rows, written packed (lmce_rmsnorm_pack); backward scatters
+    d_hidden to the unpacked rows, zero elsewhere (lmce_rmsnorm_backward)."""
+
+    @staticmethod
+    def forward(ctx, hidden, weight, eps, valid_idx):
+        hdim = hidden.shape[-1]
+        h2d = hidden.reshape(-1, hdim).contiguous()
+        w = weight.contiguous()
+        n = valid_idx.numel()
+        dev = h2d.device
+        x = torch.empty((n, hdim), dtype=h2d.dtype, device=dev)
+        rstd = torch.empty(n, dtype=torch.float32, device=dev)
+        if n > 0:
+            with torch.cuda.device(dev):
+                _lib.call("lmce_rmsnorm_pack", h2d.data_ptr(), w.data_ptr(), float(eps), valid_idx.data_ptr(), None,
+                          n, hdim, _DTYPES[h2d.dtype], x.data_ptr(), rstd.data_ptr(), _stream(dev))
+        ctx.save_for_backward(h2d, w, rstd, valid_idx)
+        ctx.shape = hidden.shape
+        return x
+
+    @staticmethod
+    def backward(ctx, dx):
+        h2d, w, rstd, valid_idx = ctx.saved_tensors
+        dh = torch.zeros_like(h2d)
+        n = valid_idx.numel()
+        if n > 0 and ctx.needs_input_grad[0]:
+            g = dx.to(h2d.dtype).contiguous()
+            with torch.cuda.device(h2d.device):
+                _lib.call("lmce_rmsnorm_backward", g.data_ptr(), h2d.data_ptr(), w.data_ptr(), rstd.data_ptr(),
+                          valid_idx.data_ptr(), None, n, h2d.shape[1], _DTYPES[h2d.dtype], dh.data_ptr(),
+                          _stream(h2d.device))
+        return dh.view(ctx.shape), None, None, None
+
+
+def rms_norm_pack(hidden: torch.Tensor, weight: torch.Tensor, packed: PackedBatch, eps: float = 1e-6):
+    """The final RMSNorm in front of the head (ops.py:824) applied to the kept rows only and
+    written packed, replacing normalise-all-then-gather; [N, H] for ``chunked_lm_head``. The
+    norm weight is frozen, as in the reference (its gradient is not computed)."""
+    if hidden.device.type != "cuda":
+        raise RuntimeError("rms_norm_pack runs on CUDA tensors only (no CPU path)")
+    if weight.requires_grad:
+        raise RuntimeError("rms_norm_pack does not compute the norm weight's gradient; pass a frozen weight")
+    return RMSNormPackFn.apply(hidden, weight, eps, packed.valid_idx)
+
+
 def lm_head_with_proxy(hidden_packed: torch.Tensor, packed: PackedBatch, weight: torch.Tensor,
                        num_items_in_batch=None, v_chunk: int | None = None, proxy_dtype=torch.float16):
     """Steps 3-4 of the reference's fused forward (ops.py:1143-1184): the head on packed
