@@ -70,3 +70,44 @@ def test_tied_gradient_time(cuda_device):
         torch.cuda.synchronize()
         times.setdefault("tied" if tied else "autograd", []).append(a.elapsed_time(b) / 10)
     print("fwd+bwd ms per step:", {k: [round(x, 3) for x in v] for k, v in times.items()})
+
+
+def test_packed_norm_tied_flow_matches_autograd(cuda_device):
+    """The flow around the head as the integration guide wires it (tied embedding -> layer
+    stand-in -> pack -> fused final RMSNorm -> head with the tied slot -> scatter), against
+    plain autograd through F.embedding, the oracle's RMSNorm and F.cross_entropy."""
+    from rus_b200 import chunked_lm_head
+    from rus_b200.packing import rms_norm_pack, scatter_head_outputs, shift_and_pack
+    from rus_b200.tied import TiedGradSlot, tied_embedding
+
+    B, S, H, V = 2, 96, 256, 5000
+    g = torch.Generator(device=cuda_device).manual_seed(11)
+    W0 = (torch.randn(V, H, device=cuda_device, generator=g) * 0.05).half()
+    ids = torch.randint(0, V, (B, S), device=cuda_device, generator=g)
+    labels = ids.clone()
+    labels[:, :10] = -100
+    mask = torch.ones(B, S, dtype=torch.long, device=cuda_device)
+    mask[1, 70:] = 0
+    labels[1, 70:] = -100
+    norm_w = (1 + 0.1 * torch.randn(H, device=cuda_device, generator=g)).half()
+
+    W = W0.clone().requires_grad_(True)
+    slot = TiedGradSlot()
+    h = tied_embedding(ids, W, slot) * 1.5 + 0.25  # stand-in for the model's layers
+    packed = shift_and_pack(labels, mask)
+    x = rms_norm_pack(h, norm_w, packed)
+    loss, nll, ent, arg = chunked_lm_head(x, packed.shift_labels, W, None, None, slot)
+    full_nll, full_ent, full_arg = scatter_head_outputs(packed, nll, ent, arg)
+    loss.backward()
+
+    Wr = W0.float().clone().requires_grad_(True)
+    hr = F.embedding(ids, Wr) * 1.5 + 0.25
+    xr, _ = orc.rms_norm_ref(hr, norm_w)
+    xk = xr.reshape(-1, H)[packed.valid_idx]
+    z = xk.half().float() @ Wr.half().float().T
+    loss_r = F.cross_entropy(z, packed.shift_labels, ignore_index=-100, reduction="sum")
+    loss_r = loss_r / (packed.shift_labels != -100).sum()
+    loss_r.backward()
+    assert abs(loss.item() - loss_r.item()) <= 2e-3 * abs(loss_r.item())
+    assert orc.rel_l2(W.grad.float(), Wr.grad) < 2e-2
+    assert full_nll.shape == (B, S) and full_arg.shape == (B, S)
