@@ -49,9 +49,9 @@ PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # DRAM bytes (read + write) of one forward-statistics launch at config 2, from one
 # `ncu --set full` capture (dram__bytes_read.sum + dram__bytes_write.sum) of the second
 # step of two config-2 steps run through chunked_lm_head.
-FWD_STATS_TRAFFIC_C2 = 503_297_000 + 5_941_000
+FWD_STATS_TRAFFIC_C2 = 503_564_000 + 6_679_000
 # DRAM bytes of one persistent backward launch at config 2 (same capture; pair kernel).
-BWD_TRAFFIC_C2 = 1_885_633_000 + 1_120_405_000
+BWD_TRAFFIC_C2 = 1_971_626_000 + 1_093_174_000
 
 
 def load_peaks():
