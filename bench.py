@@ -47,11 +47,11 @@ CONFIGS = {
 }
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # DRAM bytes (read + write) of one forward-statistics launch at config 2, from one
-# `ncu --set full` capture (dram__bytes_read.sum + dram__bytes_write.sum) of the second
-# step of two config-2 steps run through chunked_lm_head.
-FWD_STATS_TRAFFIC_C2 = 503_564_000 + 6_679_000
+# `ncu --set full` capture (dram__bytes_read.sum + dram__bytes_write.sum) of this
+# script's second warm-up step.
+FWD_STATS_TRAFFIC_C2 = 506_910_000 + 5_596_000
 # DRAM bytes of one persistent backward launch at config 2 (same capture; pair kernel).
-BWD_TRAFFIC_C2 = 1_971_626_000 + 1_093_174_000
+BWD_TRAFFIC_C2 = 1_974_155_000 + 1_095_150_000
 
 
 def load_peaks():
