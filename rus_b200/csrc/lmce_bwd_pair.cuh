@@ -3,7 +3,7 @@
 // Same work as lmce_bwd_kernel (recomputed logits -> G, dX and dW GEMMs), laid out
 // so that the two CTAs of a cluster share every tile: the MMA is 256 x N, each CTA
 // stages its 128 rows of A and N/2 rows of B (32 KB a k-block instead of 48 KB for a
-// 128 x 256 tile on one SM), six stages deep. The token rows are the N dimension of
+// 128 x 256 tile on one SM), five stages deep. The token rows are the N dimension of
 // the tiles that contract over them (a K-major B operand, any multiple of 16, used in
 // steps of 64), so they are padded to 64, not to the M tile.
 //   GT(c)   vocab block jv (M, 256) x row block i (N <= 256) of G^T = W_c . X_lab^T,
@@ -37,12 +37,13 @@ constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;       // 32 KB
 constexpr int P_RB = 256;                                  // token rows per row block
 constexpr int P_XPOSE_PITCH = 33 * 4;                      // fp32 32 x 32 transpose, conflict-free
 constexpr int P_XPOSE_BYTES = 8 * 32 * P_XPOSE_PITCH;      // per-warp slices of the eight epilogue warps
-// stages, 1 KB of barriers and ring, the staging slices, and 1 KB of slack for the
-// 1024-byte alignment of the dynamic shared memory base
 constexpr int P_ROWDATA_BYTES = P_RB * 8;                  // per-tile lse * log2(e) and chunk-local label of 256 rows
+// stages, 1 KB of barriers and ring, the staging slices, the row data, and 1 KB of slack
+// for the 1024-byte alignment of the dynamic shared memory base
 constexpr int PBWD_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 2048 + P_XPOSE_BYTES + P_ROWDATA_BYTES;
-static_assert(25 * 8 <= 256, "pair barriers end below the ring");
-static_assert(32 * ROW_STAGE_PITCH + 128 <= 32 * P_XPOSE_PITCH, "16-bit staging + row lse fit a warp's slice");
+static_assert((2 * P_STAGES + 5 + 2 * SCHED_DEPTH) * 8 <= 256, "pair barriers end below the ring");
+static_assert(32 * ROW_STAGE_PITCH <= 32 * P_XPOSE_PITCH, "16-bit staging fits a warp's slice");
+static_assert(PBWD_SMEM_BYTES <= 227 * 1024, "dynamic shared memory of one CTA");
 
 struct PairGeom {
   int n_lab, nrb, nh, C, vc, V, nX;
