@@ -67,12 +67,14 @@ def _group_name(group) -> str:
 
 
 class NvlsDxExchange:
-    """Symmetric buffers of the fused dX exchange for one (device, group, n, h, dtype):
-    the per-row-block flags, this rank's fp32 contribution and the dtype output, in one
-    allocation mapped into an NVLink multicast object on every rank of the group."""
+    """Symmetric buffers of the fused dX exchange for one (device, group, h, dtype) and up to
+    ``capacity`` tokens: the per-row-block flags, this rank's fp32 contribution and the dtype
+    output, in one allocation mapped into an NVLink multicast object on every rank of the
+    group. Calls with fewer tokens use the leading rows."""
 
     def __init__(self, buf: torch.Tensor, hdl, n: int, h: int, dtype: torch.dtype, rank: int, world: int):
         self.buf, self.hdl = buf, hdl
+        self.capacity = n
         part_off = self.flag_bytes(n, h, world)
         out_off = part_off + _round_up(4 * n * h, 256)
         base, mc = buf.data_ptr(), int(hdl.multicast_ptr)
@@ -102,30 +104,42 @@ NVLS_MIN_DX_BYTES = 32 << 20  # fp32 dX size from which the fused exchange beats
 
 
 def nvls_dx_exchange(n: int, h: int, dtype: torch.dtype, device: torch.device, group=None):
-    """The group's ``NvlsDxExchange`` for this shape, or None when the fused exchange is
-    not used: LMCE_NVLS=0, or (default) fp32 dX below NVLS_MIN_DX_BYTES, or the group
-    cannot use NVLink SHARP (decided jointly, so every rank takes the same path).
-    LMCE_NVLS=1 uses it whenever the GPUs support it. Cached per shape."""
+    """The group's ``NvlsDxExchange`` for n tokens, or None when the fused exchange is not
+    used: LMCE_NVLS=0, or (default) fp32 dX below NVLS_MIN_DX_BYTES, or the group cannot use
+    NVLink SHARP (decided jointly, so every rank takes the same path). LMCE_NVLS=1 uses it
+    whenever the GPUs support it. One buffer per (device, group, h, dtype), reused for any n
+    up to its capacity and replaced by one 1.5x larger when n outgrows it (every rank sees
+    the same n, so all ranks reallocate together)."""
     mode = os.environ.get("LMCE_NVLS", "auto")
     if mode == "0" or device.type != "cuda":
         return None
     if mode != "1" and 4 * n * h < NVLS_MIN_DX_BYTES:
         return None
-    key = (device.index, _group_name(group), n, h, dtype)
-    if key in _NVLS_CACHE:
-        return _NVLS_CACHE[key]
+    key = (device.index, _group_name(group), h, dtype)
+    cached = _NVLS_CACHE.get(key, False)
+    if cached is None:
+        return None  # the group cannot use NVLink SHARP
+    if cached is not False and cached.capacity >= n:
+        return cached
+    cap = _round_up(n, 1024) if cached is False else max(_round_up(n, 1024), _round_up(cached.capacity * 3 // 2, 1024))
+    if cached is not False:
+        # every rank's last kernel on the old buffer has finished before any rank frees it
+        torch.cuda.synchronize(device)
+        dist.barrier(group=group, device_ids=[device.index])
+        del _NVLS_CACHE[key]
+        cached = None
     state = None
     ok = 1
     try:
         import torch.distributed._symmetric_memory as symm_mem
 
         world = dist.get_world_size(group)
-        buf = symm_mem.empty(NvlsDxExchange.nbytes(n, h, world), dtype=torch.uint8, device=device)
+        buf = symm_mem.empty(NvlsDxExchange.nbytes(cap, h, world), dtype=torch.uint8, device=device)
         hdl = symm_mem.rendezvous(buf, _group_name(group))
         if int(getattr(hdl, "multicast_ptr", 0)) == 0 or int(getattr(hdl, "offset", 0)) != 0:
             ok = 0
         else:
-            state = NvlsDxExchange(buf, hdl, n, h, dtype, dist.get_rank(group), world)
+            state = NvlsDxExchange(buf, hdl, cap, h, dtype, dist.get_rank(group), world)
     except Exception:
         ok = 0
     flag = torch.tensor([ok], dtype=torch.int32, device=device)

@@ -1,7 +1,7 @@
 """GPU, 2 ranks: the vocab-sharded head against the single-GPU head, with the dX sum
 both fused into the backward kernel over NVLink SHARP (when the GPUs support it) and
-as an NCCL all-reduce. Consecutive calls with different labelled-row counts reuse the
-fused exchange's buffers.
+as an NCCL all-reduce. Consecutive calls with different labelled-row counts, and with
+fewer tokens than an earlier call, reuse the fused exchange's buffers; more tokens grow them.
 
 Runs as spawned child processes, one per GPU (skipped with fewer than 2 GPUs).
 NCCL's own NVLS is switched off (NCCL_NVLS_ENABLE=0); a short process-group timeout
@@ -41,9 +41,13 @@ def _worker(rank, world, port, q):
         ok = True
         msg = ""
         # (N, H, V, dtype, v_chunk, fraction of ignored labels per call): consecutive calls
-        # with different labelled-row counts reuse the exchange buffers of one shape
+        # with different labelled-row counts reuse the exchange buffers; the last two cases
+        # share (H, dtype) with the first: 1500 tokens outgrow its buffer (reallocated on
+        # both ranks), 300 tokens then run in the leading rows of the larger one
         cases = [(700, 512, 30011, torch.float16, 4096, (0.2, 0.2)),
-                 (1000, 1536, 20000, torch.bfloat16, 0, (0.2, 0.9, 0.0, 1.0, 0.5))]
+                 (1000, 1536, 20000, torch.bfloat16, 0, (0.2, 0.9, 0.0, 1.0, 0.5)),
+                 (1500, 512, 30011, torch.float16, 4096, (0.3,)),
+                 (300, 512, 30011, torch.float16, 0, (0.1,))]
         for ci, (N, H, V, dt, vc, masks) in enumerate(cases):
             g = torch.Generator().manual_seed(99 + ci)
             X = torch.randn(N, H, generator=g).to(dt).to(dev)
