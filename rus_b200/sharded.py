@@ -16,7 +16,8 @@ hidden states and labels are replicated. The two exchange steps:
   slice of the block's columns over the GPUs through the switch
   (``multimem.ld_reduce``) and stores the result to every GPU's output copy
   (``multimem.st``), while the last two chunks' dW tiles still compute. The
-  buffers are torch symmetric memory, allocated once per shape. Otherwise one
+  buffers are torch symmetric memory, kept per hidden size and dtype and grown
+  when a call has more tokens than they hold. Otherwise one
   NCCL all-reduce sums the fp32 contributions after the kernel and
   ``lmce_dx_finalize`` casts them to the input dtype. Measured at the config-2 shape
   (ms per step, fused / NCCL): 8 GPUs, 16384 tokens (dX 100 MB) 3.58 / 3.90; 4 GPUs,
