@@ -260,8 +260,12 @@ class FusedChunkedLMHeadFn(torch.autograd.Function):
             if dx is not None:
                 dx = dx.view(ctx.orig_shape)
         if dw is not None and ctx.tied_slot is not None:
-            # tied input embedding: its backward adds into this buffer and returns the sum
-            ctx.tied_slot.dw = dw
+            # tied input embedding: its backward adds into this buffer and returns the sum; a
+            # second head on the same slot in one backward pass adds to what is parked
+            if ctx.tied_slot.dw is None:
+                ctx.tied_slot.dw = dw
+            else:
+                ctx.tied_slot.dw.add_(dw)
             dw = None
         return dx, None, dw, None, None, None
 

@@ -8,6 +8,12 @@ the same backward pass, adds its rows into that buffer with
 ``lmce_embedding_grad_add`` (per token id, summed in fp64, one rounding) and returns
 it as the weight's only gradient. The forward lookup is ``lmce_embedding_lookup``
 (the reference's is HostHead.embed, solution/hostload.py:381-386).
+
+Several heads and embeddings may share one slot within a backward pass (micro-batches
+summed into one loss): a head adds its dW to whatever is parked, and the first
+embedding backward that runs afterwards takes the sum; the others return their own
+gradient alone, so the weight's total gradient is the same in every execution order.
+A slot passed to a head must also reach an embedding on that head's input path.
 """
 from __future__ import annotations
 

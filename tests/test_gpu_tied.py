@@ -111,3 +111,27 @@ def test_packed_norm_tied_flow_matches_autograd(cuda_device):
     assert abs(loss.item() - loss_r.item()) <= 2e-3 * abs(loss_r.item())
     assert orc.rel_l2(W.grad.float(), Wr.grad) < 2e-2
     assert full_nll.shape == (B, S) and full_arg.shape == (B, S)
+
+
+def test_two_heads_share_one_slot(cuda_device):
+    """Two micro-batches on one slot, their losses summed before one backward: the parked dW
+    values add, and the weight gradient matches plain autograd."""
+    from rus_b200 import chunked_lm_head
+    from rus_b200.tied import TiedGradSlot, tied_embedding
+
+    W0, ids, labels = _inputs(cuda_device, 1200, 256, 5000, torch.float16, seed=4)
+    halves = (slice(0, 600), slice(600, 1200))
+
+    W = W0.clone().requires_grad_(True)
+    slot = TiedGradSlot()
+    losses = [chunked_lm_head(tied_embedding(ids[s], W, slot) * k, labels[s], W, None, None, slot)[0]
+              for s, k in zip(halves, (1.5, 0.5))]
+    (losses[0] + losses[1]).backward()
+    assert slot.dw is None
+
+    Wr = W0.clone().requires_grad_(True)
+    refs = [chunked_lm_head(F.embedding(ids[s], Wr) * k, labels[s], Wr)[0] for s, k in zip(halves, (1.5, 0.5))]
+    (refs[0] + refs[1]).backward()
+    assert abs(losses[0].item() - refs[0].item()) <= 1e-6 * abs(refs[0].item())
+    # fp16 sums in a different order: a few ulps
+    assert orc.rel_l2(W.grad.float(), Wr.grad.float()) < 4e-3
