@@ -10,7 +10,7 @@ reference's dataset is not available offline). One step = loss forward + backwar
 the public autograd API. N > 1 (weak scaling, default): the head is vocab-sharded over the N GPUs and
 the global batch is N x 2048 tokens, so every GPU does the work of one config-2 step; the per-token
 statistics are all-gathered over NCCL and dX is summed inside the backward kernel over NVLink SHARP
-(fp32 dX of 64 MiB or more) or by an NCCL all-reduce. ``--scaling strong`` keeps 2048 tokens and
+(fp32 dX of 32 MiB or more) or by an NCCL all-reduce. ``--scaling strong`` keeps 2048 tokens and
 splits the vocabulary instead.
 
 ``value`` is device-timed with the inputs resident (L2 flushed between steps); ``e2e`` runs the same

@@ -76,5 +76,7 @@ class TiedEmbeddingFn(torch.autograd.Function):
 
 def tied_embedding(input_ids: torch.Tensor, weight: torch.Tensor, slot: TiedGradSlot | None = None) -> torch.Tensor:
     """Embedding lookup ``weight[input_ids]`` whose weight gradient is added into the head's dW
-    parked in ``slot`` (pass the same slot to ``chunked_lm_head``)."""
+    parked in ``slot`` (pass the same slot to ``chunked_lm_head``). Ids outside [0, V) give
+    zero rows and no gradient (the library's lookup serves vocab shards that way); unlike
+    ``F.embedding`` they are not reported, since checking would need a host read."""
     return TiedEmbeddingFn.apply(input_ids, weight, slot)
