@@ -137,12 +137,15 @@ LMCE_API int lmce_backward(const void* hidden, const void* weight, const int64_t
  * symmetric memory): the *_mc fields are multicast addresses, the others this
  * rank's own view. */
 typedef struct lmce_dx_exchange {
+  /* The buffers may be sized for any capacity >= n_tokens (rows of hidden_dim elements) and
+     reused by calls with fewer tokens: a call uses the leading rows and flag words only. */
   float* partial;          /* fp32 [n_tokens, hidden_dim]: this rank's dX contribution (scratch) */
   const float* partial_mc; /* multicast address of `partial` */
   void* out_mc;            /* dtype [n_tokens, hidden_dim]: on return every rank's copy holds the
                               summed dX rows of the labelled tokens (other rows are not written) */
   const uint32_t* flags;   /* uint32 [world + 2 * ceil(n_tokens / 256) * world * ceil(hidden_dim / 256)],
-                              zeroed on every rank (and a group barrier passed) before the first call */
+                              zeroed on every rank (and a group barrier passed) before the first call;
+                              the word of (row block m, rank, column tile) does not depend on n_tokens */
   uint32_t* flags_mc;      /* multicast address of `flags` */
   uint32_t epoch;          /* 1 on the first call with these flags, then +1 per call; equal on all ranks */
   int32_t rank, world;     /* this rank and the group size */
