@@ -101,6 +101,15 @@ def _round_up(x: int, a: int) -> int:
     return (x + a - 1) // a * a
 
 
+def exchange_capacity(n: int, current: int = 0) -> int:
+    """Token capacity of the exchange buffers for a call with n tokens when the group's current
+    buffers hold ``current`` (0: none): unchanged while n fits, else the larger of n and 1.5x the
+    current capacity, in multiples of 1024 tokens."""
+    if 0 < n <= current:
+        return current
+    return max(_round_up(max(n, 1), 1024), _round_up(current * 3 // 2, 1024))
+
+
 NVLS_MIN_DX_BYTES = 32 << 20  # fp32 dX size from which the fused exchange beats NCCL's all-reduce
 
 
@@ -122,7 +131,7 @@ def nvls_dx_exchange(n: int, h: int, dtype: torch.dtype, device: torch.device, g
         return None  # the group cannot use NVLink SHARP
     if cached is not False and cached.capacity >= n:
         return cached
-    cap = _round_up(n, 1024) if cached is False else max(_round_up(n, 1024), _round_up(cached.capacity * 3 // 2, 1024))
+    cap = exchange_capacity(n, 0 if cached is False else cached.capacity)
     if cached is not False:
         # every rank's last kernel on the old buffer has finished before any rank frees it
         torch.cuda.synchronize(device)

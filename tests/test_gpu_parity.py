@@ -176,6 +176,56 @@ def test_forward_only_and_no_grad(cuda_device):
     assert not nll.requires_grad and not arg.requires_grad
 
 
+def test_empty_batch(cuda_device):
+    """N = 0 tokens (a packed batch with nothing kept): zero loss, empty per-token outputs,
+    gradients of the right shapes and all zero."""
+    from rus_b200 import chunked_lm_head
+
+    h = torch.zeros(0, 128, dtype=torch.float16, device=cuda_device, requires_grad=True)
+    w = (torch.randn(700, 128) * 0.05).half().to(cuda_device).requires_grad_(True)
+    y = torch.zeros(0, dtype=torch.long, device=cuda_device)
+    loss, nll, ent, arg = chunked_lm_head(h, y, w)
+    loss.backward()
+    assert loss.item() == 0.0
+    assert nll.shape == (0,) and ent.shape == (0,) and arg.shape == (0,) and arg.dtype == torch.int64
+    assert h.grad.shape == (0, 128)
+    assert w.grad.shape == w.shape and float(w.grad.abs().max()) == 0.0
+
+
+def test_label_out_of_range_is_reported(cuda_device):
+    """A label that is neither -100 nor in [0, V) gives its token a NaN nll and leaves
+    LMCE_ERR_LABEL_RANGE in the device error word; the kernels only compare labels (no memory is
+    addressed by one), so the other tokens are unaffected and the backward stays finite. (The
+    reference's eager F.cross_entropy stops on a device-side assert instead.)"""
+    from rus_b200 import _lib, chunked_lm_head
+
+    g = torch.Generator().manual_seed(21)
+    n, hd, v = 96, 128, 700
+    hidden = torch.randn(n, hd, generator=g).half()
+    weight = (torch.randn(v, hd, generator=g) * 0.05).half()
+    labels = torch.randint(0, v, (n,), generator=g)
+    bad = labels.clone()
+    bad[5] = v + 3
+    bad[17] = -7
+    _lib.device_error(reset=True)
+    h = hidden.to(cuda_device).requires_grad_(True)
+    loss, nll, ent, arg = chunked_lm_head(h, bad.to(cuda_device), weight.to(cuda_device))
+    loss.backward()
+    torch.cuda.synchronize()
+    code = _lib.device_error(reset=True)
+    assert _lib.device_error(reset=True) == 0
+    assert code == _lib.LMCE_ERR_LABEL_RANGE
+    nll = nll.cpu()
+    assert bool(torch.isnan(nll[5])) and bool(torch.isnan(nll[17]))
+    keep = torch.ones(n, dtype=torch.bool)
+    keep[[5, 17]] = False
+    ref = orc.eager_head(hidden, labels, weight, grads=False)
+    assert _close_per_token(nll[keep], ref["nll"][keep]) == 0
+    ent_o, ent_r = ent.double().cpu(), ref["entropy"].double()
+    assert ((ent_o - ent_r).abs() <= 1e-3 * torch.clamp(ent_r.abs(), min=1.0)).all()
+    assert bool(torch.isfinite(h.grad).all())
+
+
 def test_timeout_path_reports_error(cuda_device):
     """A bounded wait that nothing satisfies returns LMCE_ERR_TIMEOUT instead of hanging."""
     from rus_b200 import _lib

@@ -128,3 +128,26 @@ def test_shard_range_partitions_vocab():
             assert max(sizes) - min(sizes) <= 1
     with pytest.raises(ValueError):
         shard_range(4, 0, 8)
+
+
+def test_exchange_capacity_grows_geometrically():
+    """The fused exchange's buffers keep their capacity for calls that fit and grow to at least
+    1.5x when outgrown, so a run whose token counts vary reallocates O(log) times."""
+    from rus_b200.sharded import NvlsDxExchange, exchange_capacity
+
+    assert exchange_capacity(700) == 1024
+    assert exchange_capacity(300, 1024) == 1024
+    assert exchange_capacity(1024, 1024) == 1024
+    assert exchange_capacity(1025, 1024) == 2048
+    assert exchange_capacity(1500, 2048) == 2048
+    assert exchange_capacity(5000, 2048) == 5120
+    cap, grows = 0, 0
+    for n in list(range(100, 40000, 37)):
+        new = exchange_capacity(n, cap)
+        assert new >= n and new % 1024 == 0
+        grows += new != cap
+        cap = new
+    assert grows <= 10
+    # flag words of (row block m, rank, column tile) do not depend on N: a smaller call's flags
+    # are the leading words of a larger allocation's
+    assert NvlsDxExchange.flag_bytes(300, 1536, 8) <= NvlsDxExchange.flag_bytes(2048, 1536, 8)
