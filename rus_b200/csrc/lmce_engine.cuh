@@ -144,20 +144,6 @@ __device__ __forceinline__ bool named_bar_all(bool pred) {
   return out != 0;
 }
 
-// Epilogue barrier that also returns the AND of `pred` over the 128 threads (one answer for all).
-__device__ __forceinline__ bool epilogue_bar_all(bool pred) {
-  uint32_t out;
-  asm volatile(
-      "{\n\t.reg .pred pi, po;\n\t"
-      "setp.ne.u32 pi, %1, 0;\n\t"
-      "bar.red.and.pred po, 1, 128, pi;\n\t"
-      "selp.u32 %0, 1, 0, po;\n\t}"
-      : "=r"(out)
-      : "r"(static_cast<uint32_t>(pred))
-      : "memory");
-  return out != 0;
-}
-
 // ------------------------------------------------------- operand staging ---
 
 // TMA loads of one k-block of the A (BM rows) or B (BN rows) operand into a stage.
