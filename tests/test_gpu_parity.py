@@ -83,6 +83,10 @@ EDGE_CASES = [
     (64, 64, 100, torch.float16, "all_valid"),  # V smaller than one vocab tile
     (200, 256, 4099, torch.float16, "all_masked"),
     (384, 320, 2560, torch.bfloat16, "random"),
+    # H >= 256 runs the CTA-pair backward: one labelled token, V below one vocab tile, H = 256
+    (1, 256, 1000, torch.float16, "all_valid"),
+    (70, 384, 100, torch.bfloat16, "all_valid"),
+    (300, 256, 2000, torch.float16, "random"),
 ]
 
 
