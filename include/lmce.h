@@ -173,11 +173,14 @@ LMCE_API int lmce_backward_nvls(const void* hidden, const void* weight, const in
                                 void* stream);
 
 /* d_hidden[t] = src[t] for tokens whose label is not -100, zero rows otherwise
- * ([n_tokens, hidden_dim] in dtype; the read-out of lmce_backward_nvls). */
+ * ([n_tokens, hidden_dim] in dtype; the read-out of lmce_backward_nvls). No
+ * counterpart in the reference, which is single-GPU. */
 LMCE_API int lmce_dx_copy_labelled(const void* src, const int64_t* labels, int64_t n_tokens, int64_t hidden_dim,
                                    int dtype, void* d_hidden, void* stream);
 
-/* d_hidden = dtype(d_hidden_f32), elementwise over n_tokens x hidden_dim. */
+/* d_hidden = dtype(d_hidden_f32), elementwise over n_tokens x hidden_dim: the final
+ * cast of an fp32 dX summed across GPUs (the reference's single-GPU dX leaves its
+ * fp16 accumulator through the rescale at ops.py:337-338). */
 LMCE_API int lmce_dx_finalize(const float* d_hidden_f32, int64_t n_tokens, int64_t hidden_dim, int dtype,
                      void* d_hidden, void* stream);
 
@@ -240,8 +243,10 @@ LMCE_API size_t lmce_embedding_grad_workspace_bytes(int64_t n_tokens, int64_t vo
  * weight gradient). For every position i whose token id lies in
  * [vocab_offset, vocab_offset + vocab_local):
  *   d_weight[id - vocab_offset, :] += d_embed[i, :]
- * summed per id in fp64 with the existing value and rounded once to dtype
- * (deterministic: independent of the order of positions).
+ * summed per id in fp64 with the existing value and rounded once to dtype. fp16
+ * values are multiples of 2^-24 below 2^16, so up to 8192 positions per id add
+ * exactly and the result does not depend on their order; bf16 sums are exact
+ * while one id's values in a column span less than about 2^32.
  *   d_embed    [n_tokens, hidden_dim] dtype, gradient of the lookup's output
  *   token_ids  [n_tokens] int64
  *   d_weight   [vocab_local, hidden_dim] dtype, updated in place */
