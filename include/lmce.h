@@ -96,7 +96,9 @@ LMCE_API int lmce_stats_reduce(const lmce_part* parts, int64_t n_parts, int64_t 
  * the loss reduction at ops.py:268-277):
  *   lse = m + ln s;  entropy = ln s - w / s;  nll = lse - z_y (0 when label == -100)
  *   argmax = lowest vocab id of the max logit
- *   denom = *num_items_dev if non-null, else num_items if >= 0, else #(label != -100); clamped to >= 1
+ *   denom = *num_items_dev if non-null, else num_items unless it is NaN, else #(label != -100);
+ *           clamped to >= 1 (like the reference's max(float(num_items_in_batch), 1.0), a zero or
+ *           negative count gives 1). Pass NaN for "not given".
  *   loss = sum(nll) / denom  (fixed-order reduction, deterministic)
  * Outputs: lse, nll, entropy [n_tokens] fp32; argmax [n_tokens] int64; loss, denom fp32 scalars. */
 LMCE_API int lmce_stats_finish(const lmce_part* parts, int64_t n_parts, int64_t tok_stride, int64_t part_stride,
@@ -300,6 +302,15 @@ LMCE_API uint64_t lmce_launch_count(void);
  *   which = 1: the persistent kernel of lmce_backward
  * NULL events switch recording off. The events must already exist. */
 LMCE_API int lmce_set_timing_events(int which, void* begin, void* end);
+
+/* Role counters of the CTA-pair backward kernel; no counterpart in the reference.
+ * Only a library compiled with -DLMCE_ROLE_PROFILE=1 collects them; the normal
+ * build returns LMCE_ERR_UNSUPPORTED. Copies (synchronously) up to counter_bytes of
+ * the per-CTA cycle counters (32 uint64 per CTA, slots in csrc/lmce_prof.cuh) and
+ * up to timeline_bytes of the per-tile timeline (1024 entries of 8 uint64 per CTA),
+ * then zeroes both when `reset` is non-zero. */
+LMCE_API int lmce_profile_read(void* counters, size_t counter_bytes, void* timeline, size_t timeline_bytes,
+                               int reset);
 
 /* Launches a kernel whose bounded wait is never satisfied; after timeout_ns it
  * records LMCE_ERR_TIMEOUT in the device error word and returns normally.

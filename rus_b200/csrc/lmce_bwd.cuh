@@ -45,6 +45,11 @@
 namespace lmce {
 
 constexpr int NUM_GBUF = 3;
+// G is stored prescaled by 2^15 in the input dtype: p * dnll for p ~ 1/V would underflow
+// fp16 otherwise, and |G| <= 2^15 keeps it finite (the reference's 2^16 could overflow at
+// denom 1). The dX / dW epilogues divide it out.
+constexpr float GSCALE = 32768.0f;
+constexpr float GSCALE_LOG2 = 15.0f;
 constexpr int SCHED_DEPTH = 4;
 // Per-warp staging of 32 rows x 32 columns of 16-bit output (64 bytes a row, padded to
 // 80 so the row-wise 16-byte writes of a warp hit distinct banks).
@@ -84,6 +89,7 @@ struct BwdParams {
   int x_rank, x_world;
   int x_lo, x_hi;          // this rank's column slice of H (multiples of 8)
   void* dw_out;            // [V][H] input dtype (nullable)
+  const void* w;           // [V][H] input dtype: the head rows of this shard (L2 prefetch source)
   int want_dx, want_dw;
   int mn3_h;               // X and W MN-major maps are 3-D (H a multiple of 64, H >= 256); G's always are
   const float* grad_loss;  // device scalar (nullable: 1)

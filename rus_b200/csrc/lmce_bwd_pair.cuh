@@ -4,17 +4,21 @@
 // so that the two CTAs of a cluster share every tile: the MMA is 256 x N, each CTA
 // stages its 128 rows of A and N/2 rows of B (32 KB a k-block instead of 48 KB for a
 // 128 x 256 tile on one SM), five stages deep. The token rows are the N dimension of
-// the tiles that contract over them (a K-major B operand, any multiple of 16, used in
-// steps of 64), so they are padded to 64, not to the M tile.
-//   GT(c)   vocab block jv (M, 256) x row block i (N <= 256) of G^T = W_c . X_lab^T,
+// the tiles that contract over them, so a row block's tile is 128 or 256 tokens wide
+// (padded to 128, not to the M tile). The gradient tile is stored transposed, as
+// G^T [vocab][token] (the TMEM layout: each epilogue thread holds one vocab row), so
+// the epilogue writes it without a shared-memory transpose; the dX GEMM reads it as an
+// MN-major B operand and the dW GEMM as a K-major A operand.
+//   GT(c)   vocab block jv (M, 256) x row block i (N = 128 or 256) of G^T = W_c . X_lab^T,
 //           K = H: the epilogue forms G = (softmax - onehot) * 2^15 in the input dtype
-//           and writes it, transposed through shared memory, to G buffer c % NUM_GBUF
-//           as [row][vocab] (replaces the reference's pass-2 GEMM + lm_head_piece_kernel
+//           (the prescale folded into the exponent) and writes rows of G^T to G buffer
+//           c % NUM_GBUF (replaces the reference's pass-2 GEMM + lm_head_piece_kernel
 //           MODE 1, solution/ops.py:287-319, solution/kernels.py:517-531)
 //   DXT(c)  hidden block p (M) x row block i (N) of dX^T += W_c^T . G_c^T, K = chunk
-//           width; fp32 accumulation in a [H][rows] buffer in chunk order; the last chunk
-//           scales by grad_loss / denom / 2^15, transposes through shared memory and
-//           scatters rows to token order (replaces ops.py:320 and 337-338)
+//           width; fp32 accumulation in a [H][rows] buffer in chunk order (the previous
+//           chunk's partial is loaded while the UMMAs run); the last chunk scales by
+//           grad_loss / denom / 2^15, transposes through shared memory and scatters rows
+//           to token order (replaces ops.py:320 and 337-338)
 //   DW(c)   vocab block jv (M) x hidden block p (N = 256) of dW = G_c^T . X_lab, K =
 //           labelled tokens (new: the reference returns None for the weight, ops.py:339)
 // The tile list, its order, the dependency counters and the fused cross-GPU exchange
@@ -25,24 +29,34 @@
 #pragma once
 
 #include "lmce_bwd.cuh"
+#include "lmce_prof.cuh"
 
 namespace lmce {
 
-constexpr int P_STAGES = 5;
+#ifndef LMCE_P_STAGES
+#define LMCE_P_STAGES 5
+#endif
+#ifndef LMCE_W_PREFETCH
+#define LMCE_W_PREFETCH 0
+#endif
+constexpr int P_STAGES = LMCE_P_STAGES;
+// GT tiles prefetch into L2 the W rows of the vocab block this many blocks ahead (0: off)
+constexpr int W_PREFETCH_BLOCKS = LMCE_W_PREFETCH;
 constexpr int P_THREADS = 320;  // warp 0 producer, warp 1 UMMA, warps 2-9 epilogue (two per TMEM lane quadrant)
 constexpr int P_EPI = 256;
 constexpr int P_A_BYTES = BM * BK * 2;                     // 128 rows x 64 k: 16 KB
 constexpr int P_B_BYTES = BM * BK * 2;                     // up to 128 rows (N / 2) x 64 k: 16 KB
 constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;       // 32 KB
 constexpr int P_RB = 256;                                  // token rows per row block
-constexpr int P_XPOSE_PITCH = 33 * 4;                      // fp32 32 x 32 transpose, conflict-free
-constexpr int P_XPOSE_BYTES = 8 * 32 * P_XPOSE_PITCH;      // per-warp slices of the eight epilogue warps
+constexpr int P_SLICE_BYTES = 32 * ROW_STAGE_PITCH;         // one epilogue warp's staging slice (2.5 KB)
+constexpr int P_XPOSE_PITCH = 17;                          // fp32 32 x 32 transpose in two halves, in floats
+constexpr int P_XPOSE_BYTES = 8 * P_SLICE_BYTES;           // slices of the eight epilogue warps
 constexpr int P_ROWDATA_BYTES = P_RB * 8;                  // per-tile lse * log2(e) and chunk-local label of 256 rows
 // stages, 1 KB of barriers and ring, the staging slices, the row data, and 1 KB of slack
 // for the 1024-byte alignment of the dynamic shared memory base
 constexpr int PBWD_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 2048 + P_XPOSE_BYTES + P_ROWDATA_BYTES;
 static_assert((2 * P_STAGES + 5 + 2 * SCHED_DEPTH) * 8 <= 256, "pair barriers end below the ring");
-static_assert(32 * ROW_STAGE_PITCH <= 32 * P_XPOSE_PITCH, "16-bit staging fits a warp's slice");
+static_assert(32 * P_XPOSE_PITCH * 4 <= P_SLICE_BYTES, "half-transpose staging fits a warp's slice");
 static_assert(PBWD_SMEM_BYTES <= 227 * 1024, "dynamic shared memory of one CTA");
 
 struct PairGeom {
@@ -53,11 +67,10 @@ struct PairGeom {
   __device__ __forceinline__ int nG(int c) const { return nvb(c) * nrb; }
   __device__ __forceinline__ int nDX() const { return dx ? nh * nrb : 0; }
   __device__ __forceinline__ int nDW(int c) const { return dw ? nvb(c) * nh : 0; }
-  // N of a row-block tile: the block's rows rounded up to 64
-  __device__ __forceinline__ int rows_n(int i) const {
-    const int r = n_lab - i * P_RB;
-    return r >= P_RB ? P_RB : ((r + 63) / 64) * 64;
-  }
+  // N of a row-block tile: 128 when at most 128 rows of the block hold labelled tokens,
+  // else 256 (each CTA's half of an MN-major G^T operand is then one or two whole
+  // 64-token swizzle blocks)
+  __device__ __forceinline__ int rows_n(int i) const { return n_lab - i * P_RB > BM ? P_RB : BM; }
   __device__ __forceinline__ int num_kb(const BwdTile& t, int H) const {
     if (t.kind == BK_XCH) return 0;
     if (t.kind == BK_G) return (H + BK - 1) / BK;
@@ -169,10 +182,13 @@ struct PairCursor {
 template <bool BF16, bool A_MN, bool B_MN, int NCOLS>
 __device__ __forceinline__ bool mma_tile_pair(uint8_t* smem, uint64_t* full_bar, uint64_t* empty_bar,
                                               uint32_t peer_empty, int nkb, uint32_t d_tmem, int& stage,
-                                              uint32_t& phase, volatile int* abort_flag, uint64_t tlimit) {
+                                              uint32_t& phase, volatile int* abort_flag, uint64_t tlimit,
+                                              long long& full_wait) {
   constexpr uint32_t idesc = make_idesc_f16(BF16, A_MN, B_MN, 2 * BM, NCOLS);
   for (int kb = 0; kb < nkb; ++kb) {
+    LMCE_PROF(const long long t0 = clock64();)
     if (!mbar_wait(&full_bar[stage], phase, abort_flag, tlimit)) return false;
+    LMCE_PROF(full_wait += clock64() - t0;)
     tc_fence_after();
     const uint32_t sa = smem_u32(smem + stage * P_STAGE_BYTES);
 #pragma unroll
@@ -192,33 +208,37 @@ __device__ __forceinline__ bool mma_tile_pair(uint8_t* smem, uint64_t* full_bar,
 template <bool BF16, bool A_MN, bool B_MN>
 __device__ __forceinline__ bool mma_tile_pair_n(int ncols, uint8_t* smem, uint64_t* full_bar, uint64_t* empty_bar,
                                                 uint32_t peer_empty, int nkb, uint32_t d_tmem, int& stage,
-                                                uint32_t& phase, volatile int* abort_flag, uint64_t tlimit) {
+                                                uint32_t& phase, volatile int* abort_flag, uint64_t tlimit,
+                                                long long& full_wait) {
   switch (ncols) {
-    case 64:
-      return mma_tile_pair<BF16, A_MN, B_MN, 64>(smem, full_bar, empty_bar, peer_empty, nkb, d_tmem, stage, phase,
-                                                 abort_flag, tlimit);
     case 128:
       return mma_tile_pair<BF16, A_MN, B_MN, 128>(smem, full_bar, empty_bar, peer_empty, nkb, d_tmem, stage, phase,
-                                                  abort_flag, tlimit);
-    case 192:
-      return mma_tile_pair<BF16, A_MN, B_MN, 192>(smem, full_bar, empty_bar, peer_empty, nkb, d_tmem, stage, phase,
-                                                  abort_flag, tlimit);
+                                                  abort_flag, tlimit, full_wait);
     default:
       return mma_tile_pair<BF16, A_MN, B_MN, 256>(smem, full_bar, empty_bar, peer_empty, nkb, d_tmem, stage, phase,
-                                                  abort_flag, tlimit);
+                                                  abort_flag, tlimit, full_wait);
   }
 }
 
 // 32 x 32 fp32 transpose within a warp: lane l passes its 32 values (column l of the
-// block) and receives row l (32 values).
+// block) and receives row l (32 values), in two passes through a 32 x 17 staging block:
+// lanes 16h .. 16h + 15 store theirs, then every lane reads its row's 16 values of them.
 __device__ __forceinline__ void warp_transpose32(float* stage, float* v, int lane) {
-  constexpr int P = P_XPOSE_PITCH / 4;
+  constexpr int P = P_XPOSE_PITCH;
+  float out[32];
 #pragma unroll
-  for (int j = 0; j < 32; ++j) stage[j * P + lane] = v[j];
-  __syncwarp();
+  for (int h = 0; h < 2; ++h) {
+    if ((lane >> 4) == h) {
 #pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = stage[lane * P + j];
-  __syncwarp();
+      for (int j = 0; j < 32; ++j) stage[j * P + (lane & 15)] = v[j];
+    }
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 16; ++i) out[16 * h + i] = stage[lane * P + i];
+    __syncwarp();
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = out[j];
 }
 
 template <bool BF16>
@@ -245,7 +265,7 @@ __global__ void __launch_bounds__(P_THREADS, 1)
   const int lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();  // 0 = leader
   // per-warp epilogue staging (after the 1 KB barrier block), then the GT tiles' row data
-  uint8_t* xstage = smem + P_STAGES * P_STAGE_BYTES + 1024 + (warp >= 2 ? warp - 2 : 0) * 32 * P_XPOSE_PITCH;
+  uint8_t* xstage = smem + P_STAGES * P_STAGE_BYTES + 1024 + (warp >= 2 ? warp - 2 : 0) * P_SLICE_BYTES;
   float* row_lse = reinterpret_cast<float*>(smem + P_STAGES * P_STAGE_BYTES + 1024 + P_XPOSE_BYTES);
   int* row_lbl = reinterpret_cast<int*>(row_lse + P_RB);
   const PairGeom geo = make_pair_geom(p);
@@ -292,6 +312,7 @@ __global__ void __launch_bounds__(P_THREADS, 1)
   const uint32_t tmem_base = *tmem_holder;
   const uint64_t tlimit = p.timeout_ns;
   const uint32_t leader_sched_empty = mapa_shared(smem_u32(sched_empty), 0);
+  LMCE_PROF(const long long prof_t_begin = clock64();)
 
   if (warp == 0) {
     // ------------------------------------------- scheduler + TMA producer ---
@@ -307,13 +328,16 @@ __global__ void __launch_bounds__(P_THREADS, 1)
       const uint32_t full_leader = mapa_shared(smem_u32(full_bar), 0);
       const uint32_t peer_ring = mapa_shared(smem_u32(ring), 1);
       const uint32_t peer_sched_full = mapa_shared(smem_u32(sched_full), 1);
+      LMCE_PROF(long long pc_sched = 0, pc_dep_g = 0, pc_dep_gd = 0, pc_empty = 0, pc_tiles = 0;)
       for (;;) {
         BwdTile t;
+        LMCE_PROF(long long pt0 = clock64();)
         if (rank == 0) {
           if (!mbar_wait_cluster(&sched_empty[slot], sphase ^ 1u, abort_flag, tlimit)) {
             ok = false;
             break;
           }
+          LMCE_PROF(pc_sched += clock64() - pt0; pt0 = clock64();)
           const bool has = cur.decode(geo, next_ticket, t);
           if (!has) t.kind = BK_END;
           // dependencies (before the tile is handed out, so both CTAs load after them)
@@ -324,10 +348,12 @@ __global__ void __launch_bounds__(P_THREADS, 1)
               ok = wait_counter(&consumed[prev], 2 * (geo.nDX() + geo.nDW(prev)), abort_flag, tlimit);
               if (ok) gbuf_free_chunk = t.chunk;
             }
+            LMCE_PROF(pc_dep_g += clock64() - pt0;)
           } else if ((t.kind == BK_DX || t.kind == BK_DW) && t.chunk > g_ready_chunk) {
             ok = wait_counter(&gdone[t.chunk], 2 * geo.nG(t.chunk), abort_flag, tlimit);
             if (ok) g_ready_chunk = t.chunk;
             acquired = true;
+            LMCE_PROF(pc_dep_gd += clock64() - pt0;)
           }
           if (!ok) break;
           if (acquired) asm volatile("fence.proxy.async.global;" ::: "memory");
@@ -352,6 +378,7 @@ __global__ void __launch_bounds__(P_THREADS, 1)
             ok = false;
             break;
           }
+          LMCE_PROF(pc_sched += clock64() - pt0;)
           t = read_ring(&ring[slot]);
           mbar_arrive_cluster(leader_sched_empty + 8u * slot);
           if (++slot == SCHED_DEPTH) {
@@ -366,12 +393,29 @@ __global__ void __launch_bounds__(P_THREADS, 1)
         const int nkb = geo.num_kb(t, p.H);
         const int gbuf = t.chunk % NUM_GBUF;
         const int r = static_cast<int>(rank);
+        if constexpr (W_PREFETCH_BLOCKS > 0) {
+          // The first row block's GT tile of a vocab block asks L2 for the W rows of the block
+          // W_PREFETCH_BLOCKS ahead in the same chunk (the row-block tiles of one vocab block are
+          // consecutive in the list, so this runs once per vocab block).
+          if (rank == 0 && t.kind == BK_G && t.m == 0 && t.n + W_PREFETCH_BLOCKS < geo.nvb(t.chunk)) {
+            const long long row0 = static_cast<long long>(t.chunk) * p.v_chunk +
+                                   static_cast<long long>(t.n + W_PREFETCH_BLOCKS) * P_RB;
+            const long long rows = min(static_cast<long long>(P_RB), static_cast<long long>(p.V) - row0);
+            const char* src = static_cast<const char*>(p.w) + row0 * p.H * 2;
+            const long long bytes = rows * p.H * 2;
+            for (long long off = 0; off < bytes; off += 65536)
+              l2_prefetch_bulk(src + off, static_cast<uint32_t>(min(65536ll, bytes - off)));
+          }
+        }
         const int half_n = t.kind == BK_DW ? BM : geo.rows_n(t.m) / 2;  // this CTA's share of N
+        LMCE_PROF(++pc_tiles;)
         for (int kb = 0; kb < nkb; ++kb) {
+          LMCE_PROF(const long long pe0 = clock64();)
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, tlimit)) {
             ok = false;
             break;
           }
+          LMCE_PROF(pc_empty += clock64() - pe0;)
           uint8_t* sa = smem + stage * P_STAGE_BYTES;
           uint8_t* sb = sa + P_A_BYTES;
           if (rank == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * P_STAGE_BYTES);
@@ -381,10 +425,13 @@ __global__ void __launch_bounds__(P_THREADS, 1)
             tma_load_2d_pair(sa, &map_wk, fb, k0, t.chunk * p.v_chunk + t.n * P_RB + BM * r);
             tma_load_2d_pair(sb, &map_xk, fb, k0, t.m * P_RB + half_n * r);
           } else if (t.kind == BK_DX) {
+            // B: tokens of this CTA's half as MN-major blocks of G^T (two 64-token blocks; with
+            // N = 128 the UMMA reads only the first)
             tma_load_3d_pair(sa, &map_wmn, fb, 0, t.chunk * p.v_chunk + k0, (t.n * BN + BM * r) / 64);
-            tma_load_2d_pair(sb, &map_gk, fb, k0, gbuf * p.rows_pad + t.m * P_RB + half_n * r);
+            tma_load_3d_pair(sb, &map_gmn, fb, 0, gbuf * p.v_chunk + k0, (t.m * P_RB + half_n * r) / 64);
           } else {
-            tma_load_3d_pair(sa, &map_gmn, fb, 0, gbuf * p.rows_pad + k0, (t.m * P_RB + BM * r) / 64);
+            // A: this CTA's 128 vocab rows of G^T, K-major over the tokens
+            tma_load_2d_pair(sa, &map_gk, fb, k0, gbuf * p.v_chunk + t.m * P_RB + BM * r);
             tma_load_3d_pair(sb, &map_xmn, fb, 0, k0, (t.n * BN + BM * r) / 64);
           }
           ++issued;
@@ -412,6 +459,9 @@ __global__ void __launch_bounds__(P_THREADS, 1)
           }
         }
       }
+      LMCE_PROF(prof_store(PS_P_SCHED, pc_sched); prof_store(PS_P_DEP_G, pc_dep_g);
+                prof_store(PS_P_DEP_GD, pc_dep_gd); prof_store(PS_P_EMPTY, pc_empty);
+                prof_store(PS_P_TILES, pc_tiles);)
     }
   } else if (warp == 1) {
     // -------------------------------------------------- UMMA issuer (leader) ---
@@ -421,11 +471,16 @@ __global__ void __launch_bounds__(P_THREADS, 1)
       int stage = 0, slot = 0, acc = 0;
       uint32_t phase = 0, sphase = 0, acc_phase = 0;
       bool ok = true;
+      long long full_g = 0, full_dx = 0, full_dw = 0;
+      LMCE_PROF(long long pc_msched = 0, pc_tempty = 0, kb_g = 0, kb_dx = 0, kb_dw = 0; int tl_i = 0;
+                const long long pm_loop0 = clock64();)
       for (;;) {
+        LMCE_PROF(long long pm0 = clock64();)
         if (!mbar_wait(&sched_full[slot], sphase, abort_flag, tlimit)) {
           ok = false;
           break;
         }
+        LMCE_PROF(pc_msched += clock64() - pm0;)
         const BwdTile t = read_ring(&ring[slot]);
         mbar_arrive(&sched_empty[slot]);
         if (++slot == SCHED_DEPTH) {
@@ -433,22 +488,29 @@ __global__ void __launch_bounds__(P_THREADS, 1)
           sphase ^= 1u;
         }
         if (t.kind == BK_END) break;
+        LMCE_PROF(pm0 = clock64();)
         if (!mbar_wait_cluster(&tempty_bar[acc], acc_phase ^ 1u, abort_flag, tlimit)) {
           ok = false;
           break;
         }
+        LMCE_PROF(pc_tempty += clock64() - pm0;
+                  if (unsigned long long* e = prof_entry(tl_i++)) e[4] = global_timer_ns();)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
         const int nkb = geo.num_kb(t, p.H);
-        if (t.kind == BK_G)
+        if (t.kind == BK_G) {
           ok = mma_tile_pair_n<BF16, false, false>(geo.rows_n(t.m), smem, full_bar, empty_bar, peer_empty, nkb,
-                                                   d_tmem, stage, phase, abort_flag, tlimit);
-        else if (t.kind == BK_DX)
-          ok = mma_tile_pair_n<BF16, true, false>(geo.rows_n(t.m), smem, full_bar, empty_bar, peer_empty, nkb,
-                                                  d_tmem, stage, phase, abort_flag, tlimit);
-        else if (t.kind == BK_DW)
-          ok = mma_tile_pair<BF16, true, true, BN>(smem, full_bar, empty_bar, peer_empty, nkb, d_tmem, stage, phase,
-                                                   abort_flag, tlimit);
+                                                   d_tmem, stage, phase, abort_flag, tlimit, full_g);
+          LMCE_PROF(kb_g += nkb;)
+        } else if (t.kind == BK_DX) {
+          ok = mma_tile_pair_n<BF16, true, true>(geo.rows_n(t.m), smem, full_bar, empty_bar, peer_empty, nkb,
+                                                 d_tmem, stage, phase, abort_flag, tlimit, full_dx);
+          LMCE_PROF(kb_dx += nkb;)
+        } else if (t.kind == BK_DW) {
+          ok = mma_tile_pair<BF16, false, true, BN>(smem, full_bar, empty_bar, peer_empty, nkb, d_tmem, stage, phase,
+                                                    abort_flag, tlimit, full_dw);
+          LMCE_PROF(kb_dw += nkb;)
+        }
         if (!ok) break;
         umma_commit_pair(smem_u32(&tfull_bar[acc]));  // also fires when no UMMA was issued
         umma_commit_pair(peer_tfull + 8u * acc);
@@ -464,6 +526,10 @@ __global__ void __launch_bounds__(P_THREADS, 1)
       umma_commit_pair(smem_u32(drain_bar));
       volatile int no_abort = 0;
       mbar_wait(drain_bar, 0, &no_abort, tlimit);
+      LMCE_PROF(prof_store(PS_M_SCHED, pc_msched); prof_store(PS_M_TEMPTY, pc_tempty);
+                prof_store(PS_M_FULL_G, full_g); prof_store(PS_M_FULL_DX, full_dx); prof_store(PS_M_FULL_DW, full_dw);
+                prof_store(PS_M_KB_G, kb_g); prof_store(PS_M_KB_DX, kb_dx); prof_store(PS_M_KB_DW, kb_dw);
+                prof_store(PS_M_LOOP, clock64() - pm_loop0);)
     }
   } else {
     // ---------------------------------------------------------- epilogue ---
@@ -478,11 +544,16 @@ __global__ void __launch_bounds__(P_THREADS, 1)
     int slot = 0, acc = 0;
     uint32_t sphase = 0, acc_phase = 0;
     bool ok = true;
+    LMCE_PROF(long long e_sched = 0, e_chain = 0, e_xch = 0, tf_g = 0, tf_dx = 0, tf_dw = 0, wk_g = 0, wk_dx = 0,
+              wk_dw = 0, n_g = 0, n_dx = 0, n_dw = 0;
+              int tl_i = 0; const long long pl0 = clock64(); long long pe_tile = 0; unsigned long long* tle = nullptr;)
     for (;;) {
+      LMCE_PROF(long long pe0 = clock64();)
       if (!mbar_wait_cluster(&sched_full[slot], sphase, abort_flag, tlimit)) {
         ok = false;
         break;
       }
+      LMCE_PROF(e_sched += clock64() - pe0;)
       const BwdTile t = read_ring(&ring[slot]);
       mbar_arrive_cluster(leader_sched_empty + 8u * slot);
       if (++slot == SCHED_DEPTH) {
@@ -490,11 +561,14 @@ __global__ void __launch_bounds__(P_THREADS, 1)
         sphase ^= 1u;
       }
       if (t.kind == BK_END) break;
+      LMCE_PROF(tle = et == 0 ? prof_entry(tl_i++) : nullptr;
+                if (tle) { tle[0] = t.kind; tle[1] = t.chunk; tle[2] = t.m; tle[3] = t.n; tle[5] = global_timer_ns(); })
       if (t.kind == BK_XCH) {
         if (!mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, tlimit)) {
           ok = false;
           break;
         }
+        LMCE_PROF(pe0 = clock64(); if (tle) tle[6] = global_timer_ns();)
         // this CTA sums rows [128 * rank, 128 * rank + 128) of the 256-row block (the first
         // four epilogue warps, on their own named barrier)
         if (ch == 0)
@@ -505,44 +579,62 @@ __global__ void __launch_bounds__(P_THREADS, 1)
           acc = 0;
           acc_phase ^= 1u;
         }
+        LMCE_PROF(e_xch += clock64() - pe0; if (tle) tle[7] = global_timer_ns();)
         continue;
       }
       const bool have_acc = geo.num_kb(t, p.H) > 0;
       const int w = geo.width(t.chunk);
       const int ncols = t.kind == BK_DW ? BN : geo.rows_n(t.m);
       const int row_blk0 = t.m * P_RB;  // first token row of a GT / DXT tile
+      const int c_lo = ch * (ncols / 64), c_hi = (ch + 1) * (ncols / 64);  // this warp's 32-column chunks
 
       if (t.kind == BK_G) {
         // row data of the tile's 256 rows, loaded while the UMMAs still run: lse * log2(e)
-        // (+inf for rows past the labelled ones, so their probabilities are 0) and the label
-        // relative to the chunk (-1: none). The previous GT tile's readers are past the
-        // barrier of its publish step.
+        // minus log2 of the G prescale (so the exponential yields p * 2^15 directly; +inf for
+        // rows past the labelled ones, so their G is 0) and the label relative to the chunk
+        // (-1: none). The previous GT tile's readers are past the barrier of its publish step.
         for (int r = et; r < P_RB; r += P_EPI) {
           const int row = row_blk0 + r;
           const bool ok_r = row < geo.n_lab;
-          row_lse[r] = ok_r ? p.lse_lab[row] * LOG2E : INFINITY;
+          row_lse[r] = ok_r ? fmaf(p.lse_lab[row], LOG2E, -GSCALE_LOG2) : INFINITY;
           const int y = ok_r ? p.lbl_lab[row] : -1;
           row_lbl[r] = y >= 0 ? y - t.chunk * p.v_chunk : -1;
         }
         named_bar<1, P_EPI>();
       }
+      // DXT: this thread's row of the fp32 accumulator dX^T[h][rows]; the previous chunk's
+      // partial of its first 32 columns is loaded while the UMMAs still run
+      const int h_dx = t.n * BN + lrow;
+      float* acc_row = p.dx_acc + static_cast<size_t>(h_dx) * p.rows_pad + row_blk0;
+      const bool dx_prev = t.kind == BK_DX && t.chunk > 0 && h_dx < p.H;
+      float4 pre[8];
       if (t.kind == BK_DX && t.chunk > 0) {
+        LMCE_PROF(pe0 = clock64();)
         // dX^T columns of this tile were last written by DXT(chunk - 1) on some pair
         if (et == 0 && !wait_counter(&dxchain[t.m * geo.nh + t.n], 2 * t.chunk, abort_flag, tlimit)) {
           raise_error(p.err, ERR_TIMEOUT);
           *abort_flag = 1;
         }
         named_bar<1, P_EPI>();
+        LMCE_PROF(e_chain += clock64() - pe0;)
+        if (dx_prev) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) pre[j] = __ldcg(reinterpret_cast<const float4*>(acc_row + c_lo * 32) + j);
+        }
       }
+      LMCE_PROF(pe0 = clock64();)
       if (!mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, tlimit)) {
         ok = false;
         break;
       }
+      LMCE_PROF(const long long dtf = clock64() - pe0; pe_tile = clock64();
+                if (t.kind == BK_G) tf_g += dtf; else if (t.kind == BK_DX) tf_dx += dtf; else tf_dw += dtf;
+                if (tle) tle[6] = global_timer_ns();)
       tc_fence_after();
       const uint32_t taddr = tmem_base + lane_base + static_cast<uint32_t>(acc * BN);
 
 #pragma unroll 1
-      for (int c = ch * (ncols / 64); c < (ch + 1) * (ncols / 64); ++c) {
+      for (int c = c_lo; c < c_hi; ++c) {
         uint32_t raw[32];
         float v[32];
         __syncwarp();
@@ -553,67 +645,52 @@ __global__ void __launch_bounds__(P_THREADS, 1)
 
         if (t.kind == BK_G) {
           // this thread: vocab row vloc of the chunk; columns: token rows row_blk0 + c * 32 + j,
-          // whose lse comes from the tile's row data (four rows per shared-memory load). The
-          // one-hot term is checked only when a label of the 32 rows falls in this warp's 32
-          // vocab rows (a ballot; rare for wide vocab chunks).
+          // whose exponent offset comes from the tile's row data (four rows per shared-memory
+          // load). The one-hot term is checked only when a label of the 32 rows falls in this
+          // warp's 32 vocab rows (a ballot; rare for wide vocab chunks). The warp's 32 rows of
+          // G^T (64 bytes each) go out through its staging slice, 8 rows x 64 bytes per store.
           const int vloc = t.n * P_RB + lrow;
           const int vbase = vloc - lane;
           const float* lse_s = row_lse + c * 32;
           const int y_l = row_lbl[c * 32 + lane];
           const bool hit = __ballot_sync(0xffffffffu, y_l >= vbase && y_l < vbase + 32) != 0u;
-          const float gs = vloc < w ? p.gscale : 0.0f;
-          uint16_t* st16 = reinterpret_cast<uint16_t*>(xstage);
+          const bool in_chunk = vloc < w;  // rows past the chunk's last vocab row store zeros
 #pragma unroll
           for (int j4 = 0; j4 < 8; ++j4) {
             const float4 L = reinterpret_cast<const float4*>(lse_s)[j4];
             const float lj[4] = {L.x, L.y, L.z, L.w};
-            float g4[4];
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
               const int j = 4 * j4 + u;
-              float pr = ex2_approx(fmaf(round_to_input<BF16>(v[j]), LOG2E, -lj[u]));
+              float pr = ex2_approx(fmaf(round_to_input<BF16>(v[j]), LOG2E, -lj[u]));  // p * 2^15
               if (hit) {  // warp-uniform
-                if (__shfl_sync(0xffffffffu, y_l, j) == vloc) pr -= 1.0f;
+                if (__shfl_sync(0xffffffffu, y_l, j) == vloc) pr -= GSCALE;
               }
-              g4[u] = pr * gs;
-            }
-            // staging rows 4 * j4 .. + 3 (tokens), column lane (vocab); one conversion per two values
-#pragma unroll
-            for (int u = 0; u < 4; u += 2) {
-              const uint32_t two = pack2<BF16>(g4[u], g4[u + 1]);
-              st16[(4 * j4 + u) * (ROW_STAGE_PITCH / 2) + lane] = static_cast<uint16_t>(two & 0xffffu);
-              st16[(4 * j4 + u + 1) * (ROW_STAGE_PITCH / 2) + lane] = static_cast<uint16_t>(two >> 16);
+              v[j] = in_chunk ? pr : 0.0f;
             }
           }
-          __syncwarp();
-          // copy out: 8 token rows x 64 bytes (32 vocab columns) per instruction
           char* gbase = reinterpret_cast<char*>(p.g) +
-                        (static_cast<size_t>(t.chunk % NUM_GBUF) * p.rows_pad * p.v_chunk + t.n * P_RB +
-                         BM * static_cast<int>(rank) + q * 32) * 2;
-#pragma unroll
-          for (int i2 = 0; i2 < 4; ++i2) {
-            const int rr = i2 * 8 + (lane >> 2);
-            const int piece = lane & 3;
-            const uint4 u = *reinterpret_cast<const uint4*>(xstage + rr * ROW_STAGE_PITCH + piece * 16);
-            *reinterpret_cast<uint4*>(gbase + static_cast<size_t>(row_blk0 + c * 32 + rr) * p.v_chunk * 2 +
-                                      piece * 16) = u;
-          }
-          __syncwarp();
+                        ((static_cast<size_t>(t.chunk % NUM_GBUF) * p.v_chunk + vbase) * p.rows_pad + row_blk0 +
+                         c * 32) * 2;
+          store_rows32<BF16>(xstage, v, gbase, static_cast<size_t>(p.rows_pad) * 2, 0, lane,
+                             [](int) { return true; });
         } else if (t.kind == BK_DX) {
-          // this thread: hidden index h; columns: token rows (compacted) row_blk0 + c * 32 + j
-          const int h = t.n * BN + lrow;
-          if (h < p.H) {
+          // this thread: hidden index h_dx; columns: token rows (compacted) row_blk0 + c * 32 + j
+          if (h_dx < p.H) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] *= dscale;
-            float* accp = p.dx_acc + static_cast<size_t>(h) * p.rows_pad + row_blk0 + c * 32;
-            if (t.chunk > 0) {
+            float* accp = acc_row + c * 32;
+            if (dx_prev) {
 #pragma unroll
-              for (int j = 0; j < 32; j += 4) {
-                const float4 a4 = __ldcg(reinterpret_cast<const float4*>(accp + j));
-                v[j] += a4.x;
-                v[j + 1] += a4.y;
-                v[j + 2] += a4.z;
-                v[j + 3] += a4.w;
+              for (int j = 0; j < 8; ++j) {
+                v[4 * j] += pre[j].x;
+                v[4 * j + 1] += pre[j].y;
+                v[4 * j + 2] += pre[j].z;
+                v[4 * j + 3] += pre[j].w;
+              }
+              if (c + 1 < c_hi) {  // the next chunk's partial, in flight during this chunk's stores
+#pragma unroll
+                for (int j = 0; j < 8; ++j) pre[j] = __ldcg(reinterpret_cast<const float4*>(accp + 32) + j);
               }
             }
             if (t.chunk + 1 < geo.C) {
@@ -683,11 +760,22 @@ __global__ void __launch_bounds__(P_THREADS, 1)
         __threadfence();
         atomicAdd(&consumed[t.chunk], 1);
       }
+      LMCE_PROF(const long long dwk = clock64() - pe_tile;
+                if (t.kind == BK_G) { wk_g += dwk; ++n_g; } else if (t.kind == BK_DX) { wk_dx += dwk; ++n_dx; }
+                else { wk_dw += dwk; ++n_dw; }
+                if (tle) tle[7] = global_timer_ns();)
     }
     if (!ok) {
       raise_error(p.err, ERR_TIMEOUT);
       *abort_flag = 1;
     }
+    LMCE_PROF(if (et == 0) {
+      prof_store(PS_E_SCHED, e_sched); prof_store(PS_E_CHAIN, e_chain); prof_store(PS_E_XCH, e_xch);
+      prof_store(PS_E_TFULL_G, tf_g); prof_store(PS_E_TFULL_DX, tf_dx); prof_store(PS_E_TFULL_DW, tf_dw);
+      prof_store(PS_E_WORK_G, wk_g); prof_store(PS_E_WORK_DX, wk_dx); prof_store(PS_E_WORK_DW, wk_dw);
+      prof_store(PS_E_N_G, n_g); prof_store(PS_E_N_DX, n_dx); prof_store(PS_E_N_DW, n_dw);
+      prof_store(PS_E_LOOP, clock64() - pl0);
+    })
     if (geo.xch && blockIdx.x == 0) {
       if (et == 0 && geo.nX == 0) multimem_st_release_b32(p.x_flags_mc + p.x_rank, p.x_epoch);
       for (int r = et; r < p.x_world; r += P_EPI) {
@@ -703,6 +791,7 @@ __global__ void __launch_bounds__(P_THREADS, 1)
   __syncthreads();
   cluster_sync();  // the leader's UMMAs into the peer's TMEM have drained
   tc_fence_after();
+  LMCE_PROF(if (threadIdx.x == 0) prof_store(PS_TOTAL, clock64() - prof_t_begin);)
   if (warp == 1) {
     __syncwarp();
     tmem_dealloc_pair(tmem_base, TMEM_COLS);

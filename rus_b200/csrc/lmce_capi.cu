@@ -460,7 +460,9 @@ __global__ void __launch_bounds__(1024) loss_kernel(const float* __restrict__ nl
       cnt += __shfl_down_sync(0xffffffffu, cnt, off);
     }
     if (threadIdx.x == 0) {
-      float d = num_items_dev ? *num_items_dev : (num_items >= 0.f ? num_items : static_cast<float>(cnt));
+      // num_items NaN: not given (the count of labelled tokens); any other value is used as
+      // given, then clamped to >= 1 like the reference's max(float(num_items_in_batch), 1.0)
+      float d = num_items_dev ? *num_items_dev : (isnan(num_items) ? static_cast<float>(cnt) : num_items);
       d = fmaxf(d, 1.0f);
       *denom_out = d;
       *loss = sum / d;
@@ -810,24 +812,27 @@ int backward_impl(const void* hidden, const void* weight, const int64_t* labels,
   const bool want_dw = d_weight != nullptr;
   if (!want_dx && !want_dw) return LMCE_OK;
 
-  // Tensor maps (tile offsets are TMA coordinates). The three G buffers are one
-  // [NUM_GBUF * rows_pad, v_chunk] tensor; buffer b starts at row b * rows_pad.
-  // MN-major operands load through 3-D maps (one TMA instruction per operand and k-block
-  // instead of one per 64 columns; the producer thread's issue rate bounds the DX and DW
-  // tiles otherwise).
+  // Tensor maps (tile offsets are TMA coordinates). MN-major operands load through 3-D
+  // maps (one TMA instruction per operand and k-block instead of one per 64 columns; the
+  // producer thread's issue rate bounds the DX and DW tiles otherwise). The three G
+  // buffers are one tensor: for the CTA-pair kernel G^T [NUM_GBUF * v_chunk, rows_pad]
+  // (buffer b starts at vocab row b * v_chunk), for the one-CTA kernel G
+  // [NUM_GBUF * rows_pad, v_chunk] (buffer b starts at token row b * rows_pad).
   CUtensorMap maps[6];
   const int g_rows = NUM_GBUF * L.rows_pad;
+  const int gt_rows = NUM_GBUF * L.v_chunk;
   const bool pair = use_pair_backward(h);
   const bool mn3_h = h % 64 == 0 && h >= kBN;
   if (pair) {
-    // W K-major, W MN-major, X K-major, X MN-major, G K-major, G MN-major; every box is
-    // one CTA's half of a pair tile (128 rows, or two 64-column MN blocks)
+    // W K-major, W MN-major, X K-major, X MN-major, G^T K-major (over tokens), G^T MN-major
+    // (over tokens); every box is one CTA's half of a pair tile (128 rows, or two 64-column
+    // MN blocks)
     if (int rc = make_map(&maps[0], weight, bf16, h, vl, h, BM)) return rc;
     if (int rc = make_map_mn3(&maps[1], weight, bf16, h, vl, h, BM / 64)) return rc;
     if (int rc = make_map(&maps[2], x_lab, bf16, h, L.rows_pad, h, BM)) return rc;
     if (int rc = make_map_mn3(&maps[3], x_lab, bf16, h, L.rows_pad, h, BM / 64)) return rc;
-    if (int rc = make_map(&maps[4], g, bf16, L.v_chunk, g_rows, L.v_chunk, BM)) return rc;
-    if (int rc = make_map_mn3(&maps[5], g, bf16, L.v_chunk, g_rows, L.v_chunk, BM / 64)) return rc;
+    if (int rc = make_map(&maps[4], g, bf16, L.rows_pad, gt_rows, L.rows_pad, BM)) return rc;
+    if (int rc = make_map_mn3(&maps[5], g, bf16, L.rows_pad, gt_rows, L.rows_pad, BM / 64)) return rc;
   } else {
     // x K-major, x MN-major, W K-major, W MN-major, G K-major, G MN-major (X and W fall
     // back to 2-D MN-major maps when H is below 256)
@@ -874,12 +879,13 @@ int backward_impl(const void* hidden, const void* weight, const int64_t* labels,
     p.x_hi = groups * (xch->rank + 1) / xch->world * 8;
   }
   p.dw_out = d_weight;
+  p.w = weight;
   p.want_dx = want_dx ? 1 : 0;
   p.want_dw = want_dw ? 1 : 0;
   p.mn3_h = mn3_h ? 1 : 0;
   p.grad_loss = grad_loss;
   p.denom = denom;
-  p.gscale = 32768.0f;
+  p.gscale = GSCALE;
   p.sync = sync;
   p.err = d->err_ptr;
   p.timeout_ns = wait_timeout_ns();
@@ -1128,6 +1134,30 @@ int lmce_selftest_wait_timeout(uint64_t timeout_ns, void* stream) {
 
 uint64_t lmce_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
+int lmce_profile_read(void* counters, size_t counter_bytes, void* timeline, size_t timeline_bytes, int reset) {
+#if LMCE_ROLE_PROFILE
+  if (counter_bytes > sizeof(g_prof_ctr) || timeline_bytes > sizeof(g_prof_tl))
+    return fail(LMCE_ERR_INVALID_ARGUMENT, "profile buffers larger than the device arrays");
+  if (counters && counter_bytes) LMCE_CUDA(cudaMemcpyFromSymbol(counters, g_prof_ctr, counter_bytes));
+  if (timeline && timeline_bytes) LMCE_CUDA(cudaMemcpyFromSymbol(timeline, g_prof_tl, timeline_bytes));
+  if (reset) {
+    void* p = nullptr;
+    LMCE_CUDA(cudaGetSymbolAddress(&p, g_prof_ctr));
+    LMCE_CUDA(cudaMemset(p, 0, sizeof(g_prof_ctr)));
+    LMCE_CUDA(cudaGetSymbolAddress(&p, g_prof_tl));
+    LMCE_CUDA(cudaMemset(p, 0, sizeof(g_prof_tl)));
+  }
+  return LMCE_OK;
+#else
+  (void)counters;
+  (void)counter_bytes;
+  (void)timeline;
+  (void)timeline_bytes;
+  (void)reset;
+  return fail(LMCE_ERR_UNSUPPORTED, "built without LMCE_ROLE_PROFILE");
+#endif
+}
+
 int lmce_set_timing_events(int which, void* begin, void* end) {
   if (which < 0 || which > 1) return fail(LMCE_ERR_INVALID_ARGUMENT, "timing slot %d", which);
   if ((begin == nullptr) != (end == nullptr)) return fail(LMCE_ERR_INVALID_ARGUMENT, "set both events or neither");
@@ -1188,6 +1218,13 @@ extern "C" int lmce_forward_noalloc(const void* hidden, const void* weight, cons
                                     double num_items, float* lse, float* nll, float* entropy, int64_t* argmax,
                                     float* loss, float* denom, void* stream) {
   constexpr int64_t kMaxRecords = static_cast<int64_t>(LMCE_NOALLOC_SCRATCH_BYTES / sizeof(lmce_part));
+  // every argument is checked before anything is queued, so a rejected call leaves the
+  // shared scratch (the previous call's records) untouched
+  if (!hidden || !weight || !labels || !lse || !nll || !entropy || !argmax || !loss || !denom)
+    return fail(LMCE_ERR_INVALID_ARGUMENT, "null pointer");
+  if (!aligned16(hidden) || !aligned16(weight)) return fail(LMCE_ERR_INVALID_ARGUMENT, "hidden/weight not 16-byte aligned");
+  if (dtype != LMCE_DTYPE_F16 && dtype != LMCE_DTYPE_BF16) return fail(LMCE_ERR_UNSUPPORTED, "dtype %d", dtype);
+  if (hidden_dim <= 0 || hidden_dim % 64 != 0) return fail(LMCE_ERR_UNSUPPORTED, "hidden_dim must be a positive multiple of 64");
   if (n_tokens <= 0) return fail(LMCE_ERR_INVALID_ARGUMENT, "bad n_tokens %lld", (long long)n_tokens);
   if (n_tokens > kMaxRecords)
     return fail(LMCE_ERR_INVALID_ARGUMENT,

@@ -143,6 +143,13 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
+// Asynchronous prefetch of `bytes` (a multiple of 16) of global memory at `src` (16-byte
+// aligned) into L2; nothing is written to shared memory and no barrier is signalled.
+__device__ __forceinline__ void l2_prefetch_bulk(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes)
+               : "memory");
+}
+
 // ---------------------------------------------------------------- tcgen05 ---
 
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {

@@ -71,12 +71,12 @@ def _check_inputs(hidden: torch.Tensor, labels: torch.Tensor, weight: torch.Tens
 
 
 def _denom_args(num_items_in_batch, device: torch.device):
-    """(device pointer or None, host value or -1, keep-alive tensor)."""
+    """(device pointer or None, host value or NaN for "not given", keep-alive tensor)."""
     if num_items_in_batch is None:
-        return None, -1.0, None
+        return None, float("nan"), None
     if isinstance(num_items_in_batch, torch.Tensor):
         t = num_items_in_batch.detach().to(device=device, dtype=torch.float32).reshape(1).contiguous()
-        return t.data_ptr(), -1.0, t
+        return t.data_ptr(), float("nan"), t
     return None, float(num_items_in_batch), None
 
 

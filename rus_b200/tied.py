@@ -13,7 +13,11 @@ Several heads and embeddings may share one slot within a backward pass (micro-ba
 summed into one loss): a head adds its dW to whatever is parked, and the first
 embedding backward that runs afterwards takes the sum; the others return their own
 gradient alone, so the weight's total gradient is the same in every execution order.
-A slot passed to a head must also reach an embedding on that head's input path.
+A slot passed to a head must also reach an embedding on that head's input path: if a
+backward pass parks a dW that no embedding backward collects (the head's input was
+detached, or the embedding sits in another graph), the next forward through the slot
+raises instead of adding that stale gradient into the next step's. A slot serves one
+forward/backward at a time; micro-batches whose backward passes overlap need a slot each.
 """
 from __future__ import annotations
 
@@ -33,6 +37,12 @@ class TiedGradSlot:
 class TiedEmbeddingFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, input_ids, weight, slot):
+        if slot is not None and slot.dw is not None:
+            raise RuntimeError(
+                "tied_embedding: the slot still holds a head gradient from an earlier backward pass that "
+                "no embedding backward collected (was the head's input detached from this embedding?); "
+                "it would be added into this step's gradient. Clear it (slot.dw = None) or use one slot "
+                "per forward/backward.")
         if weight.device.type != "cuda":
             raise RuntimeError("tied_embedding runs on CUDA tensors only (no CPU path)")
         ids = input_ids.contiguous().view(-1).to(torch.int64)

@@ -41,17 +41,24 @@ def _close_per_token(ours, ref, rtol=1e-3, floor=1e-3):
     return int(bad.sum())
 
 
-def _check_contract(ours, ref, logits32, dtype, check_dw=True):
+def _check_contract(ours, ref, logits32, dtype, check_dw=True, label=""):
+    """The north-star bars; returns the argmax report (printed with the case label)."""
     assert torch.isfinite(ours["loss"]).item()
     assert _close_per_token(ours["loss"].reshape(1), ref["loss"].reshape(1)) == 0, (ours["loss"], ref["loss"])
     assert _close_per_token(ours["nll"], ref["nll"]) == 0
     ent_o, ent_r = ours["entropy"].double().cpu(), ref["entropy"].double().cpu()
     assert ((ent_o - ent_r).abs() <= 1e-3 * torch.clamp(ent_r.abs(), min=1.0)).all()
-    ok = orc.argmax_mismatch_ok(ours["argmax"], ref["argmax"], logits32, dtype)
-    assert bool(ok.all()), f"{int((~ok).sum())} argmax mismatches beyond the tie rule"
-    assert orc.rel_l2(ours["dX"].float(), ref["dX"].float()) < 1e-2
+    rep = orc.argmax_tie_report(ours["argmax"], ref["argmax"], logits32, dtype)
+    print(f"argmax {label}: " + ", ".join(f"{k} {v}" for k, v in rep.items() if k != "ok"))
+    # every mismatch is accepted by the tie rule, and every accepted one is a near-tie at the top
+    assert rep["rejected"] == 0, f"{rep['rejected']} argmax mismatches beyond the tie rule"
+    assert rep["not_top"] == 0, f"{rep['not_top']} accepted argmax mismatches away from the row maximum"
+    dx_err = orc.rel_l2(ours["dX"].float(), ref["dX"].float())
+    assert dx_err < 1e-2, dx_err
     if check_dw:
-        assert orc.rel_l2(ours["dW"].float(), ref["dW"].float()) < 1e-2
+        dw_err = orc.rel_l2(ours["dW"].float(), ref["dW"].float())
+        assert dw_err < 1e-2, dw_err
+    return rep
 
 
 def test_reference_known_answer(cuda_device):
@@ -116,16 +123,21 @@ def test_edge_cases(cuda_device, n, h, v, dtype, pattern):
     _check_contract(ours, ref, logits32, dtype)
 
 
-@pytest.mark.parametrize("kind", ["int", "tensor"])
+@pytest.mark.parametrize("kind", ["int", "tensor", "zero", "negative"])
 def test_num_items_in_batch(cuda_device, kind):
+    """denom = num_items_in_batch clamped to >= 1 (ops.py:268-277: max(float(n), 1.0)), so a zero
+    or negative count divides by 1, not by the number of labelled tokens."""
     g = torch.Generator().manual_seed(11)
     n, h, v = 96, 128, 3000
     hidden = torch.randn(n, h, generator=g).half()
     weight = (torch.randn(v, h, generator=g) * 0.05).half()
     labels = torch.randint(0, v, (n,), generator=g)
     labels[::3] = -100
-    num_items = 500 if kind == "int" else torch.tensor(500, device=cuda_device)
-    ref = orc.eager_head(hidden, labels, weight, num_items_in_batch=500, grad_mode="fp32")
+    host = {"int": 500, "tensor": 500, "zero": 0, "negative": -7}[kind]
+    num_items = torch.tensor(host, device=cuda_device) if kind == "tensor" else host
+    ref = orc.eager_head(hidden, labels, weight, num_items_in_batch=host, grad_mode="fp32")
+    if kind in ("zero", "negative"):
+        assert ref["denom"] == 1.0
     ours = _run_ours(hidden.to(cuda_device), labels.to(cuda_device), weight.to(cuda_device), num_items=num_items)
     _check_contract(ours, ref, hidden.float() @ weight.float().t(), torch.float16)
 
@@ -145,15 +157,41 @@ def test_v_chunk_invariance(cuda_device, v_chunk):
     assert torch.equal(a["argmax"], b["argmax"])
 
 
-@pytest.mark.parametrize("cfg,n_override", [("c1", None), ("c5", 600), ("c4", 256), ("c3", 256)])
+@pytest.mark.parametrize("cfg,n_override", [("c1", None), ("c5", 600), ("c5", None), ("c4", 256), ("c3", 256)])
 def test_config_parity(cuda_device, cfg, n_override):
-    """BASELINE.json configs (full H and V), against the reference eager path run on the GPU."""
+    """BASELINE.json configs (full H and V), against the reference eager path run on the GPU.
+    ("c5", None) is the numerics-stress config at its full size (~2.7k tokens, three rows all
+    ignored, logit std ~12, exact top-2 ties on 1% of the tokens)."""
     X, y, W, meta = orc.make_config_inputs(cfg, seed=0, device="cpu", n_override=n_override)
     Xd, yd, Wd = X.to(cuda_device), y.to(cuda_device), W.to(cuda_device)
     ref = orc.eager_head(Xd, yd, Wd, grad_mode="fp32")
     ours = _run_ours(Xd, yd, Wd)
     logits32 = (Xd.float() @ Wd.float().t())
-    _check_contract(ours, ref, logits32, X.dtype)
+    rep = _check_contract(ours, ref, logits32, X.dtype, label=f"{cfg} N={meta['N']}")
+    if cfg == "c5":
+        # the planted exact ties (two identical W rows, so identical fp32 logits in any
+        # accumulation order) resolve to the lower index, as in the reference's argmax
+        top = logits32.max(dim=1).values
+        at_top = logits32 == top[:, None]
+        tied = at_top.sum(1) > 1
+        assert int(tied.sum()) >= max(1, meta["N"] // 200)
+        first = torch.argmax(at_top.to(torch.int8), dim=1)
+        assert torch.equal(ours["argmax"][tied].cpu(), first[tied].cpu())
+    del logits32
+
+
+@pytest.mark.parametrize("cfg", ["c1", "c2", "c5"])
+def test_bench_workload_parity(cuda_device, cfg):
+    """The exact inputs bench.py times (bench.make_config on the GPU, single GPU, the library's
+    default vocab chunk), against the reference eager path on the GPU; c2 is the benchmark's
+    headline workload (N=2048, H=1536, V=151936, fp16)."""
+    import bench
+
+    X, y, W, lens = bench.make_config(cfg, cuda_device)
+    ref = orc.eager_head(X, y, W, grad_mode="fp32")
+    ours = _run_ours(X, y, W)  # v_chunk None: the library's default, as in the benchmark
+    logits32 = X.float() @ W.float().t()
+    _check_contract(ours, ref, logits32, X.dtype, label=f"bench {cfg} N={X.shape[0]}")
     del logits32
 
 
@@ -162,7 +200,7 @@ def test_c1_against_cpu_oracle(cuda_device):
     X, y, W, meta = orc.make_config_inputs("c1", seed=0)
     ref = orc.eager_head(X, y, W, grad_mode="fp32")
     ours = _run_ours(X.to(cuda_device), y.to(cuda_device), W.to(cuda_device))
-    _check_contract(ours, ref, X.float() @ W.float().t(), X.dtype)
+    _check_contract(ours, ref, X.float() @ W.float().t(), X.dtype, label="c1 vs CPU oracle")
 
 
 def test_forward_only_and_no_grad(cuda_device):
@@ -290,7 +328,7 @@ def test_full_size_configs(cuda_device, cfg):
     ours = _run_ours(Xd, yd, Wd)
     ref = orc.eager_head(Xd, yd, Wd, grad_mode="fp32")
     logits32 = Xd.float() @ Wd.float().t()
-    _check_contract(ours, ref, logits32, Xd.dtype)
+    _check_contract(ours, ref, logits32, Xd.dtype, label=f"{cfg} full")
     del logits32, ref
     ignored = (yd == -100)
     if bool(ignored.any()):

@@ -108,3 +108,33 @@ def test_config_generators():
     X, y, W, meta = orc.make_config_inputs("c5", seed=0, n_override=400)
     assert W.shape == (151936, 896)
     assert (y == -100).sum() > 0
+    # config 5 at full size: Zipf(1.2) lengths truncated to 1..512 (E[N] ~ 2.8k), three rows all
+    # ignored, and the exact top-2 ties (duplicated W rows) present
+    X, y, W, meta = orc.make_config_inputs("c5", seed=0)
+    assert 1500 <= meta["N"] <= 4500 and max(meta["lens"]) <= 512 and min(meta["lens"]) >= 1
+    starts = [0]
+    for L in meta["lens"][:-1]:
+        starts.append(starts[-1] + L)
+    full_rows = sum(bool((y[s0:s0 + L] == -100).all()) for s0, L in zip(starts, meta["lens"]))
+    assert full_rows >= 3
+    assert len(torch.unique(W, dim=0)) < W.shape[0]
+
+
+def test_argmax_tie_report_classifies_mismatches():
+    """The argmax report sorts mismatches by the rule that accepts them and flags any accepted
+    mismatch whose candidates are not at the top of the row (planted here on the CPU)."""
+    z = torch.tensor([[5.0, 5.0004, 1.0, 0.0],     # strict tie (gap 4e-4 < 1e-3)
+                      [40.0, 40.02, 3.0, 0.0],     # within one fp16 ulp at 40 (0.03125), > 1e-3
+                      [2.0, 9.0, 1.0, 0.0],        # real disagreement: rejected
+                      [1.0, 0.5, 0.2, 0.0]])       # exact match
+    ref = torch.tensor([1, 1, 1, 0])
+    ours = torch.tensor([0, 0, 0, 0])
+    rep = orc.argmax_tie_report(ours, ref, z, torch.float16)
+    assert (rep["exact"], rep["strict"], rep["widened"], rep["rejected"]) == (1, 1, 1, 1)
+    assert rep["not_top"] == 0
+    assert rep["ok"].tolist() == [True, True, False, True]
+    # a near-tie between two candidates far below the row maximum is accepted by the gap
+    # alone but is not a tie at the top: not_top counts it
+    z2 = torch.tensor([[10.0, 3.0, 3.0004, 0.0]])
+    rep2 = orc.argmax_tie_report(torch.tensor([1]), torch.tensor([2]), z2, torch.float16)
+    assert rep2["strict"] == 1 and rep2["not_top"] == 1

@@ -7,7 +7,10 @@ the library keeps its per-token partial records in a fixed 8 MiB device array of
 its own. This test calls that entry point through the C ABI twice in a row, with
 different inputs, and checks each result against the regular entry points
 (lmce_fwd_stats into a caller buffer + lmce_stats_finish) at the tolerances the
-other parity tests use. The file is named so pytest collects it last.
+other parity tests use; it also runs a token count large enough that the entry
+point must use fewer vocab slabs than the regular path to fit the array, and
+checks that a call after the first allocates no device memory. The file is named
+so pytest collects it last.
 """
 from __future__ import annotations
 
@@ -20,6 +23,7 @@ from rus_b200 import _lib
 
 pytestmark = pytest.mark.gpu
 
+NAN = float("nan")  # num_items not given
 DT = {torch.float16: _lib.LMCE_DTYPE_F16, torch.bfloat16: _lib.LMCE_DTYPE_BF16}
 
 
@@ -37,17 +41,17 @@ def _regular(lib, X, W, y, stream):
     o = _outputs(n, X.device)
     _lib.check(lib.lmce_fwd_stats(X.data_ptr(), W.data_ptr(), y.data_ptr(), n, h, v, 0, DT[X.dtype],
                                   parts.data_ptr(), parts_n, stream))
-    _lib.check(lib.lmce_stats_finish(parts.data_ptr(), parts_n, parts_n, 1, y.data_ptr(), n, None, -1.0,
+    _lib.check(lib.lmce_stats_finish(parts.data_ptr(), parts_n, parts_n, 1, y.data_ptr(), n, None, NAN,
                                      o["lse"].data_ptr(), o["nll"].data_ptr(), o["ent"].data_ptr(),
                                      o["arg"].data_ptr(), o["loss"].data_ptr(), o["denom"].data_ptr(), stream))
     return o
 
 
-def _noalloc(lib, X, W, y, stream):
+def _noalloc(lib, X, W, y, stream, o=None):
     n, h = X.shape
     v = W.shape[0]
-    o = _outputs(n, X.device)
-    _lib.check(lib.lmce_forward_noalloc(X.data_ptr(), W.data_ptr(), y.data_ptr(), n, h, v, DT[X.dtype], None, -1.0,
+    o = _outputs(n, X.device) if o is None else o
+    _lib.check(lib.lmce_forward_noalloc(X.data_ptr(), W.data_ptr(), y.data_ptr(), n, h, v, DT[X.dtype], None, NAN,
                                         o["lse"].data_ptr(), o["nll"].data_ptr(), o["ent"].data_ptr(),
                                         o["arg"].data_ptr(), o["loss"].data_ptr(), o["denom"].data_ptr(), stream))
     return o
@@ -93,6 +97,50 @@ def test_noalloc_rejects_sizes_beyond_scratch():
         pytest.skip("no CUDA device")
     lib = _lib.load()
     too_many = (8 << 20) // _lib.PART_BYTES + 1
-    rc = lib.lmce_forward_noalloc(16, 16, 16, too_many, 64, 100, 0, None, -1.0, 16, 16, 16, 16, 16, 16, None)
+    rc = lib.lmce_forward_noalloc(16, 16, 16, too_many, 64, 100, 0, None, NAN, 16, 16, 16, 16, 16, 16, None)
     assert rc == _lib.LMCE_ERR_INVALID_ARGUMENT
     assert b"no-allocation scratch" in ctypes.string_at(lib.lmce_last_error())
+
+
+def test_noalloc_caps_vocab_slabs_to_fit_the_scratch():
+    """Tens of thousands of tokens with a small head: the regular path would write more
+    n_tokens x slabs records than the 8 MiB array holds, so the entry point merges fewer,
+    longer vocab slabs per token; the results must not change."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    n, h, v = 60000, 64, 4096
+    cap = (8 << 20) // _lib.PART_BYTES // n
+    assert lib.lmce_fwd_num_parts(n, v) > cap, "this shape must take the slab-capping branch"
+    X, W, y = _inputs(303, n, h, v, torch.float16, dev)
+    got = _noalloc(lib, X, W, y, stream)
+    ref = _regular(lib, X, W, y, stream)
+    torch.cuda.synchronize()
+    assert _lib.device_error(reset=True) == 0
+    _assert_close(got, ref)
+
+
+def test_noalloc_call_allocates_no_device_memory():
+    """After a first call on the device (which looks up the array's address and loads the
+    kernels), a call changes neither the caching allocator's counters nor the device's free
+    memory: it runs without any allocation."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    X, W, y = _inputs(404, 1500, 512, 20000, torch.bfloat16, dev)
+    o = _outputs(X.shape[0], dev)
+    _noalloc(lib, X, W, y, stream, o)  # first call on this shape
+    torch.cuda.synchronize()
+    count0 = torch.cuda.memory_stats(dev).get("allocation.all.allocated", 0)
+    free0 = torch.cuda.mem_get_info(dev)[0]
+    _noalloc(lib, X, W, y, stream, o)
+    torch.cuda.synchronize()
+    assert torch.cuda.memory_stats(dev).get("allocation.all.allocated", 0) == count0
+    assert torch.cuda.mem_get_info(dev)[0] == free0
+    assert _lib.device_error(reset=True) == 0
