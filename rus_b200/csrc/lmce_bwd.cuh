@@ -89,7 +89,6 @@ struct BwdParams {
   int x_rank, x_world;
   int x_lo, x_hi;          // this rank's column slice of H (multiples of 8)
   void* dw_out;            // [V][H] input dtype (nullable)
-  const void* w;           // [V][H] input dtype: the head rows of this shard (L2 prefetch source)
   int want_dx, want_dw;
   int mn3_h;               // X and W MN-major maps are 3-D (H a multiple of 64, H >= 256); G's always are
   const float* grad_loss;  // device scalar (nullable: 1)

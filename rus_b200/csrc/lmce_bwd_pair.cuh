@@ -2,9 +2,11 @@
 //
 // Same work as lmce_bwd_kernel (recomputed logits -> G, dX and dW GEMMs), laid out
 // so that the two CTAs of a cluster share every tile: the MMA is 256 x N, each CTA
-// stages its 128 rows of A and N/2 rows of B (32 KB a k-block instead of 48 KB for a
-// 128 x 256 tile on one SM), five stages deep. The token rows are the N dimension of
-// the tiles that contract over them, so a row block's tile is 128 or 256 tokens wide
+// stages its 128 rows of A and N/2 rows of B. A stage holds K = 128 (64 KB per CTA,
+// three stages), and each operand of a stage arrives as one TMA box that reads 256
+// contiguous bytes of each of its 128 rows, which keeps the pair UMMA fed (about 63
+// bytes per clock per SM, where 128-byte rows give 46-52). The token rows are the N
+// dimension of the tiles that contract over them, so a row block's tile is 128 or 256 tokens wide
 // (padded to 128, not to the M tile). The gradient tile is stored transposed, as
 // G^T [vocab][token] (the TMEM layout: each epilogue thread holds one vocab row), so
 // the epilogue writes it without a shared-memory transpose; the dX GEMM reads it as an
@@ -15,10 +17,11 @@
 //           c % NUM_GBUF (replaces the reference's pass-2 GEMM + lm_head_piece_kernel
 //           MODE 1, solution/ops.py:287-319, solution/kernels.py:517-531)
 //   DXT(c)  hidden block p (M) x row block i (N) of dX^T += W_c^T . G_c^T, K = chunk
-//           width; fp32 accumulation in a [H][rows] buffer in chunk order (the previous
-//           chunk's partial is loaded while the UMMAs run); the last chunk scales by
-//           grad_loss / denom / 2^15, transposes through shared memory and scatters rows
-//           to token order (replaces ops.py:320 and 337-338)
+//           width; fp32 accumulation in a [H][rows] buffer in chunk order: TMA stores
+//           (chunk 0) and TMA adds (later chunks) of 32 x 32 boxes; the last chunk reads
+//           the sum back, adds its own, scales by grad_loss / denom / 2^15, transposes
+//           through shared memory and scatters rows to token order (replaces ops.py:320
+//           and 337-338)
 //   DW(c)   vocab block jv (M) x hidden block p (N = 256) of dW = G_c^T . X_lab, K =
 //           labelled tokens (new: the reference returns None for the weight, ops.py:339)
 // The tile list, its order, the dependency counters and the fused cross-GPU exchange
@@ -33,30 +36,35 @@
 
 namespace lmce {
 
-#ifndef LMCE_P_STAGES
-#define LMCE_P_STAGES 5
-#endif
-#ifndef LMCE_W_PREFETCH
-#define LMCE_W_PREFETCH 0
-#endif
-constexpr int P_STAGES = LMCE_P_STAGES;
-// GT tiles prefetch into L2 the W rows of the vocab block this many blocks ahead (0: off)
-constexpr int W_PREFETCH_BLOCKS = LMCE_W_PREFETCH;
+// A stage holds K = 128 of both operands (two 64-element swizzle blocks), and every
+// operand arrives as one 3-D TMA box {64, 128, 2} that reads 256 contiguous bytes of
+// each of its 128 rows: measured on B200 at ~63 bytes per clock per SM against ~46 for
+// two 2-D {64, 128} boxes (128 bytes per row), while a 256 x 256 pair UMMA consumes 64.
+constexpr int P_KB = 2 * BK;     // K per stage
+constexpr int P_STAGES = 3;
 constexpr int P_THREADS = 320;  // warp 0 producer, warp 1 UMMA, warps 2-9 epilogue (two per TMEM lane quadrant)
 constexpr int P_EPI = 256;
-constexpr int P_A_BYTES = BM * BK * 2;                     // 128 rows x 64 k: 16 KB
-constexpr int P_B_BYTES = BM * BK * 2;                     // up to 128 rows (N / 2) x 64 k: 16 KB
-constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;       // 32 KB
+constexpr int P_A_BYTES = BM * P_KB * 2;                   // 128 rows x 128 k: 32 KB
+constexpr int P_B_BYTES = BM * P_KB * 2;                   // up to 128 rows (N / 2) x 128 k: 32 KB
+constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;       // 64 KB
+constexpr int P_BLOCK_BYTES = BM * BK * 2;                 // one 64-element block of a 128-row operand: 16 KB
 constexpr int P_RB = 256;                                  // token rows per row block
-constexpr int P_SLICE_BYTES = 32 * ROW_STAGE_PITCH;         // one epilogue warp's staging slice (2.5 KB)
+// One epilogue warp's staging slice: a 32 x 32 fp32 block in the 128-byte swizzled layout
+// of a TMA box (4 KB, 1024-byte aligned), also used for 16-bit row staging and transposes.
+constexpr int P_SLICE_BYTES = 32 * 32 * 4;
 constexpr int P_XPOSE_PITCH = 17;                          // fp32 32 x 32 transpose in two halves, in floats
 constexpr int P_XPOSE_BYTES = 8 * P_SLICE_BYTES;           // slices of the eight epilogue warps
-constexpr int P_ROWDATA_BYTES = P_RB * 8;                  // per-tile lse * log2(e) and chunk-local label of 256 rows
-// stages, 1 KB of barriers and ring, the staging slices, the row data, and 1 KB of slack
-// for the 1024-byte alignment of the dynamic shared memory base
-constexpr int PBWD_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 2048 + P_XPOSE_BYTES + P_ROWDATA_BYTES;
+// A GT tile's per-row data (exponent offset and chunk-local label) for the 128 token
+// columns a warp handles, kept in the warp's slice behind its 16-bit row staging.
+constexpr int P_ROWDATA_OFF = 32 * ROW_STAGE_PITCH;        // 2560
+static_assert(P_ROWDATA_OFF + 128 * 8 <= P_SLICE_BYTES, "row data fits behind the row staging");
+// stages, 1 KB of barriers and ring, the staging slices, and 1 KB of slack for the
+// 1024-byte alignment of the dynamic shared memory base
+constexpr int PBWD_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 2048 + P_XPOSE_BYTES;
 static_assert((2 * P_STAGES + 5 + 2 * SCHED_DEPTH) * 8 <= 256, "pair barriers end below the ring");
 static_assert(32 * P_XPOSE_PITCH * 4 <= P_SLICE_BYTES, "half-transpose staging fits a warp's slice");
+static_assert(32 * ROW_STAGE_PITCH <= P_SLICE_BYTES, "16-bit row staging fits a warp's slice");
+static_assert((P_STAGES * P_STAGE_BYTES + 1024) % 1024 == 0, "staging slices are 1024-byte aligned (128-byte swizzle)");
 static_assert(PBWD_SMEM_BYTES <= 227 * 1024, "dynamic shared memory of one CTA");
 
 struct PairGeom {
@@ -71,11 +79,12 @@ struct PairGeom {
   // else 256 (each CTA's half of an MN-major G^T operand is then one or two whole
   // 64-token swizzle blocks)
   __device__ __forceinline__ int rows_n(int i) const { return n_lab - i * P_RB > BM ? P_RB : BM; }
+  // stages (K = 128 each) of a tile; a stage past the end of K reads zeros (TMA fill)
   __device__ __forceinline__ int num_kb(const BwdTile& t, int H) const {
     if (t.kind == BK_XCH) return 0;
-    if (t.kind == BK_G) return (H + BK - 1) / BK;
-    if (t.kind == BK_DX) return (width(t.chunk) + BK - 1) / BK;
-    return (n_lab + BK - 1) / BK;
+    if (t.kind == BK_G) return (H + P_KB - 1) / P_KB;
+    if (t.kind == BK_DX) return (width(t.chunk) + P_KB - 1) / P_KB;
+    return (n_lab + P_KB - 1) / P_KB;
   }
 };
 
@@ -177,6 +186,16 @@ struct PairCursor {
   }
 };
 
+// Descriptor of UMMA k-step k (0..7, K = 16 each) of a 128-row operand staged by one
+// {64, 128, 2} box. K-major: two 16 KB blocks of 128 rows x 64 k (rows 128 bytes apart,
+// SBO 1024 per 8 rows), k-step k in block k / 4 at 32 bytes per step. MN-major: two
+// 64-element MN blocks 16 KB apart (LBO) of 128 k-rows of 128 bytes (SBO 1024 per 8
+// k-rows), k-step k at 16 k-rows = 2048 bytes per step.
+__device__ __forceinline__ uint64_t pair_operand_desc(uint32_t base, bool mn_major, int k) {
+  return mn_major ? smem_desc_sw128(base + k * (UMMA_K * 128), P_BLOCK_BYTES, 1024)
+                  : smem_desc_sw128(base + (k >> 2) * P_BLOCK_BYTES + (k & 3) * (UMMA_K * 2), 16, 1024);
+}
+
 // Pair UMMA k-loop of one tile (leader only); the instruction descriptor is a template
 // constant (see mma_tile). Both CTAs' empty barriers are signalled per stage.
 template <bool BF16, bool A_MN, bool B_MN, int NCOLS>
@@ -192,8 +211,8 @@ __device__ __forceinline__ bool mma_tile_pair(uint8_t* smem, uint64_t* full_bar,
     tc_fence_after();
     const uint32_t sa = smem_u32(smem + stage * P_STAGE_BYTES);
 #pragma unroll
-    for (int k = 0; k < BK / UMMA_K; ++k)
-      umma_f16_ss_pair(d_tmem, operand_desc(sa, A_MN, k), operand_desc(sa + P_A_BYTES, B_MN, k), idesc,
+    for (int k = 0; k < P_KB / UMMA_K; ++k)
+      umma_f16_ss_pair(d_tmem, pair_operand_desc(sa, A_MN, k), pair_operand_desc(sa + P_A_BYTES, B_MN, k), idesc,
                        (kb | k) != 0 ? 1u : 0u);
     umma_commit_pair(smem_u32(&empty_bar[stage]));
     umma_commit_pair(peer_empty + 8u * stage);
@@ -243,9 +262,8 @@ __device__ __forceinline__ void warp_transpose32(float* stage, float* v, int lan
 
 template <bool BF16>
 __global__ void __launch_bounds__(P_THREADS, 1)
-    lmce_bwd_pair_kernel(const __grid_constant__ CUtensorMap map_wk, const __grid_constant__ CUtensorMap map_wmn,
-                         const __grid_constant__ CUtensorMap map_xk, const __grid_constant__ CUtensorMap map_xmn,
-                         const __grid_constant__ CUtensorMap map_gk, const __grid_constant__ CUtensorMap map_gmn,
+    lmce_bwd_pair_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
+                         const __grid_constant__ CUtensorMap map_g, const __grid_constant__ CUtensorMap map_dx,
                          const BwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -266,8 +284,8 @@ __global__ void __launch_bounds__(P_THREADS, 1)
   const uint32_t rank = cluster_rank();  // 0 = leader
   // per-warp epilogue staging (after the 1 KB barrier block), then the GT tiles' row data
   uint8_t* xstage = smem + P_STAGES * P_STAGE_BYTES + 1024 + (warp >= 2 ? warp - 2 : 0) * P_SLICE_BYTES;
-  float* row_lse = reinterpret_cast<float*>(smem + P_STAGES * P_STAGE_BYTES + 1024 + P_XPOSE_BYTES);
-  int* row_lbl = reinterpret_cast<int*>(row_lse + P_RB);
+  float* row_lse = reinterpret_cast<float*>(xstage + P_ROWDATA_OFF);  // this warp's 128 token columns
+  int* row_lbl = reinterpret_cast<int*>(row_lse + 128);
   const PairGeom geo = make_pair_geom(p);
   int* ticket = p.sync;
   int* gdone = p.sync + 1;
@@ -294,12 +312,10 @@ __global__ void __launch_bounds__(P_THREADS, 1)
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&map_wk);
-    tma_prefetch_desc(&map_wmn);
-    tma_prefetch_desc(&map_xk);
-    tma_prefetch_desc(&map_xmn);
-    tma_prefetch_desc(&map_gk);
-    tma_prefetch_desc(&map_gmn);
+    tma_prefetch_desc(&map_w);
+    tma_prefetch_desc(&map_x);
+    tma_prefetch_desc(&map_g);
+    tma_prefetch_desc(&map_dx);
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_holder, TMEM_COLS);
@@ -393,20 +409,6 @@ __global__ void __launch_bounds__(P_THREADS, 1)
         const int nkb = geo.num_kb(t, p.H);
         const int gbuf = t.chunk % NUM_GBUF;
         const int r = static_cast<int>(rank);
-        if constexpr (W_PREFETCH_BLOCKS > 0) {
-          // The first row block's GT tile of a vocab block asks L2 for the W rows of the block
-          // W_PREFETCH_BLOCKS ahead in the same chunk (the row-block tiles of one vocab block are
-          // consecutive in the list, so this runs once per vocab block).
-          if (rank == 0 && t.kind == BK_G && t.m == 0 && t.n + W_PREFETCH_BLOCKS < geo.nvb(t.chunk)) {
-            const long long row0 = static_cast<long long>(t.chunk) * p.v_chunk +
-                                   static_cast<long long>(t.n + W_PREFETCH_BLOCKS) * P_RB;
-            const long long rows = min(static_cast<long long>(P_RB), static_cast<long long>(p.V) - row0);
-            const char* src = static_cast<const char*>(p.w) + row0 * p.H * 2;
-            const long long bytes = rows * p.H * 2;
-            for (long long off = 0; off < bytes; off += 65536)
-              l2_prefetch_bulk(src + off, static_cast<uint32_t>(min(65536ll, bytes - off)));
-          }
-        }
         const int half_n = t.kind == BK_DW ? BM : geo.rows_n(t.m) / 2;  // this CTA's share of N
         LMCE_PROF(++pc_tiles;)
         for (int kb = 0; kb < nkb; ++kb) {
@@ -420,19 +422,21 @@ __global__ void __launch_bounds__(P_THREADS, 1)
           uint8_t* sb = sa + P_A_BYTES;
           if (rank == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * P_STAGE_BYTES);
           const uint32_t fb = full_leader + 8u * stage;
-          const int k0 = kb * BK;
+          // every operand: one {64, 128, 2} box of a 3-D view {64 elements, rows, 64-element
+          // blocks}; K-major operands take two k-blocks of 128 rows, MN-major ones 128 k-rows
+          // of two MN blocks
           if (t.kind == BK_G) {
-            tma_load_2d_pair(sa, &map_wk, fb, k0, t.chunk * p.v_chunk + t.n * P_RB + BM * r);
-            tma_load_2d_pair(sb, &map_xk, fb, k0, t.m * P_RB + half_n * r);
+            tma_load_3d_pair(sa, &map_w, fb, 0, t.chunk * p.v_chunk + t.n * P_RB + BM * r, 2 * kb);
+            tma_load_3d_pair(sb, &map_x, fb, 0, t.m * P_RB + half_n * r, 2 * kb);
           } else if (t.kind == BK_DX) {
             // B: tokens of this CTA's half as MN-major blocks of G^T (two 64-token blocks; with
             // N = 128 the UMMA reads only the first)
-            tma_load_3d_pair(sa, &map_wmn, fb, 0, t.chunk * p.v_chunk + k0, (t.n * BN + BM * r) / 64);
-            tma_load_3d_pair(sb, &map_gmn, fb, 0, gbuf * p.v_chunk + k0, (t.m * P_RB + half_n * r) / 64);
+            tma_load_3d_pair(sa, &map_w, fb, 0, t.chunk * p.v_chunk + kb * P_KB, (t.n * BN + BM * r) / 64);
+            tma_load_3d_pair(sb, &map_g, fb, 0, gbuf * p.v_chunk + kb * P_KB, (t.m * P_RB + half_n * r) / 64);
           } else {
             // A: this CTA's 128 vocab rows of G^T, K-major over the tokens
-            tma_load_2d_pair(sa, &map_gk, fb, k0, gbuf * p.v_chunk + t.m * P_RB + BM * r);
-            tma_load_3d_pair(sb, &map_xmn, fb, 0, k0, (t.n * BN + BM * r) / 64);
+            tma_load_3d_pair(sa, &map_g, fb, 0, gbuf * p.v_chunk + t.m * P_RB + BM * r, 2 * kb);
+            tma_load_3d_pair(sb, &map_x, fb, 0, kb * P_KB, (t.n * BN + BM * r) / 64);
           }
           ++issued;
           if (++stage == P_STAGES) {
@@ -589,24 +593,28 @@ __global__ void __launch_bounds__(P_THREADS, 1)
       const int c_lo = ch * (ncols / 64), c_hi = (ch + 1) * (ncols / 64);  // this warp's 32-column chunks
 
       if (t.kind == BK_G) {
-        // row data of the tile's 256 rows, loaded while the UMMAs still run: lse * log2(e)
-        // minus log2 of the G prescale (so the exponential yields p * 2^15 directly; +inf for
-        // rows past the labelled ones, so their G is 0) and the label relative to the chunk
-        // (-1: none). The previous GT tile's readers are past the barrier of its publish step.
-        for (int r = et; r < P_RB; r += P_EPI) {
-          const int row = row_blk0 + r;
+        // row data of this warp's token columns, loaded into its slice while the UMMAs still
+        // run: lse * log2(e) minus log2 of the G prescale (so the exponential yields p * 2^15
+        // directly; +inf for rows past the labelled ones, so their G is 0) and the label
+        // relative to the chunk (-1: none)
+        for (int i = lane; i < (c_hi - c_lo) * 32; i += 32) {
+          const int row = row_blk0 + c_lo * 32 + i;
           const bool ok_r = row < geo.n_lab;
-          row_lse[r] = ok_r ? fmaf(p.lse_lab[row], LOG2E, -GSCALE_LOG2) : INFINITY;
+          row_lse[i] = ok_r ? fmaf(p.lse_lab[row], LOG2E, -GSCALE_LOG2) : INFINITY;
           const int y = ok_r ? p.lbl_lab[row] : -1;
-          row_lbl[r] = y >= 0 ? y - t.chunk * p.v_chunk : -1;
+          row_lbl[i] = y >= 0 ? y - t.chunk * p.v_chunk : -1;
         }
-        named_bar<1, P_EPI>();
+        __syncwarp();
       }
-      // DXT: this thread's row of the fp32 accumulator dX^T[h][rows]; the previous chunk's
-      // partial of its first 32 columns is loaded while the UMMAs still run
+      // DXT: this thread's row h_dx of the fp32 accumulator dX^T[h][rows]. Chunks before the
+      // last leave their partial sums to the memory system (a TMA store for chunk 0, TMA
+      // adds after it, in chunk order through dxchain). The last chunk reads the sum of the
+      // others back (the first 32 columns while the UMMAs still run), adds its own and
+      // writes dX in token order.
       const int h_dx = t.n * BN + lrow;
+      const bool dx_last = t.kind == BK_DX && t.chunk + 1 == geo.C;
       float* acc_row = p.dx_acc + static_cast<size_t>(h_dx) * p.rows_pad + row_blk0;
-      const bool dx_prev = t.kind == BK_DX && t.chunk > 0 && h_dx < p.H;
+      const bool dx_prev = dx_last && t.chunk > 0 && h_dx < p.H;
       float4 pre[8];
       if (t.kind == BK_DX && t.chunk > 0) {
         LMCE_PROF(pe0 = clock64();)
@@ -617,6 +625,7 @@ __global__ void __launch_bounds__(P_THREADS, 1)
         }
         named_bar<1, P_EPI>();
         LMCE_PROF(e_chain += clock64() - pe0;)
+        if (!dx_last && lane == 0) fence_async_global();  // the acquired sum, before this warp's TMA adds
         if (dx_prev) {
 #pragma unroll
           for (int j = 0; j < 8; ++j) pre[j] = __ldcg(reinterpret_cast<const float4*>(acc_row + c_lo * 32) + j);
@@ -651,8 +660,8 @@ __global__ void __launch_bounds__(P_THREADS, 1)
           // G^T (64 bytes each) go out through its staging slice, 8 rows x 64 bytes per store.
           const int vloc = t.n * P_RB + lrow;
           const int vbase = vloc - lane;
-          const float* lse_s = row_lse + c * 32;
-          const int y_l = row_lbl[c * 32 + lane];
+          const float* lse_s = row_lse + (c - c_lo) * 32;
+          const int y_l = row_lbl[(c - c_lo) * 32 + lane];
           const bool hit = __ballot_sync(0xffffffffu, y_l >= vbase && y_l < vbase + 32) != 0u;
           const bool in_chunk = vloc < w;  // rows past the chunk's last vocab row store zeros
 #pragma unroll
@@ -674,12 +683,33 @@ __global__ void __launch_bounds__(P_THREADS, 1)
                          c * 32) * 2;
           store_rows32<BF16>(xstage, v, gbase, static_cast<size_t>(p.rows_pad) * 2, 0, lane,
                              [](int) { return true; });
+        } else if (t.kind == BK_DX && !dx_last) {
+          // this warp's 32 hidden rows x 32 token columns, scaled, into its slice in the 128-byte
+          // swizzled box layout (16-byte piece i of row r at position i ^ (r % 8): conflict-free),
+          // then one TMA store / add of the box into dX^T
+          float4* sl = reinterpret_cast<float4*>(xstage);
+          if (c > c_lo && lane == 0) bulk_wait_read_all();  // the previous chunk's box has left the slice
+          __syncwarp();
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            sl[lane * 8 + (i ^ (lane & 7))] =
+                make_float4(v[4 * i] * dscale, v[4 * i + 1] * dscale, v[4 * i + 2] * dscale, v[4 * i + 3] * dscale);
+          fence_async_shared();
+          __syncwarp();
+          const int by = t.n * BN + BM * static_cast<int>(rank) + q * 32;  // first hidden row of the box
+          if (lane == 0 && by < p.H) {  // H is a multiple of 64: a box lies wholly inside or past H
+            const int bx = row_blk0 + c * 32;                               // token column
+            if (t.chunk == 0)
+              tma_store_2d(&map_dx, xstage, bx, by);
+            else
+              tma_reduce_add_2d(&map_dx, xstage, bx, by);
+            bulk_commit_group();
+          }
         } else if (t.kind == BK_DX) {
-          // this thread: hidden index h_dx; columns: token rows (compacted) row_blk0 + c * 32 + j
+          // last chunk: this thread: hidden index h_dx; columns: token rows (compacted) row_blk0 + c * 32 + j
           if (h_dx < p.H) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] *= dscale;
-            float* accp = acc_row + c * 32;
             if (dx_prev) {
 #pragma unroll
               for (int j = 0; j < 8; ++j) {
@@ -688,18 +718,14 @@ __global__ void __launch_bounds__(P_THREADS, 1)
                 v[4 * j + 2] += pre[j].z;
                 v[4 * j + 3] += pre[j].w;
               }
-              if (c + 1 < c_hi) {  // the next chunk's partial, in flight during this chunk's stores
+              if (c + 1 < c_hi) {  // the next 32 columns' sum, in flight during this chunk's work
 #pragma unroll
-                for (int j = 0; j < 8; ++j) pre[j] = __ldcg(reinterpret_cast<const float4*>(accp + 32) + j);
+                for (int j = 0; j < 8; ++j)
+                  pre[j] = __ldcg(reinterpret_cast<const float4*>(acc_row + (c + 1) * 32) + j);
               }
             }
-            if (t.chunk + 1 < geo.C) {
-#pragma unroll
-              for (int j = 0; j < 32; j += 4)
-                __stcg(reinterpret_cast<float4*>(accp + j), make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
-            }
           }
-          if (t.chunk + 1 == geo.C) {
+          {
             // transpose: lane l gets token row row_blk0 + c * 32 + l, hidden h0 .. h0 + 31
             warp_transpose32(reinterpret_cast<float*>(xstage), v, lane);
             const int h0 = t.n * BN + BM * static_cast<int>(rank) + q * 32;
@@ -736,6 +762,10 @@ __global__ void __launch_bounds__(P_THREADS, 1)
         acc_phase ^= 1u;
       }
       // publish this CTA's half of the tile
+      if (t.kind == BK_DX && !dx_last && lane == 0) {
+        bulk_wait_all();       // this warp's TMA stores / adds of the tile are done in global memory
+        fence_async_global();  // and ordered before the publishing thread's fence and count
+      }
       named_bar<1, P_EPI>();  // all of this CTA's stores of the tile happen before its count
       if (t.kind == BK_G) {
         if (et == 0) {
@@ -765,6 +795,7 @@ __global__ void __launch_bounds__(P_THREADS, 1)
                 else { wk_dw += dwk; ++n_dw; }
                 if (tle) tle[7] = global_timer_ns();)
     }
+    if (lane == 0) bulk_wait_all();  // no TMA store may still read the slice when the CTA exits
     if (!ok) {
       raise_error(p.err, ERR_TIMEOUT);
       *abort_flag = 1;

@@ -168,6 +168,43 @@ int make_map_mn3(CUtensorMap* m, const void* base, bool bf16, uint64_t inner, ui
   return LMCE_OK;
 }
 
+// Row-major 2-D fp32 tensor [outer][inner], box {box_inner, box_outer}, 128-byte swizzle
+// (box_inner * 4 must be 128), for TMA stores and adds.
+int make_map_f32(CUtensorMap* m, void* base, uint64_t inner, uint64_t outer, uint64_t ld_elems, uint32_t box_inner,
+                 uint32_t box_outer) {
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0) return fail(LMCE_ERR_INVALID_ARGUMENT, "tensor base not 16B aligned");
+  if ((ld_elems * 4) % 16 != 0) return fail(LMCE_ERR_INVALID_ARGUMENT, "row stride not a multiple of 16 bytes");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld_elems * 4};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(LMCE_ERR_CUDA, "cuTensorMapEncodeTiled (fp32) failed (%d)", static_cast<int>(r));
+  return LMCE_OK;
+}
+
+// The same [outer][inner] tensor of 16-bit elements as a 3-D view {64 elements, outer,
+// inner / 64 blocks at a 128-byte stride}, box {64, box_y, box_z}, 128-byte swizzle: a box
+// reads box_z * 128 contiguous bytes of each of its box_y rows.
+int make_map_3d(CUtensorMap* m, const void* base, bool bf16, uint64_t inner, uint64_t outer, uint64_t ld_elems,
+                uint32_t box_y, uint32_t box_z) {
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0) return fail(LMCE_ERR_INVALID_ARGUMENT, "tensor base not 16B aligned");
+  if ((ld_elems * 2) % 16 != 0) return fail(LMCE_ERR_INVALID_ARGUMENT, "row stride not a multiple of 16 bytes");
+  if (inner % 64 != 0) return fail(LMCE_ERR_INVALID_ARGUMENT, "3-D operand map needs a multiple of 64 columns");
+  cuuint64_t dims[3] = {64, outer, inner / 64};
+  cuuint64_t strides[2] = {ld_elems * 2, 128};
+  cuuint32_t box[3] = {64, box_y, box_z};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                        const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(LMCE_ERR_CUDA, "cuTensorMapEncodeTiled (3-D) failed (%d)", static_cast<int>(r));
+  return LMCE_OK;
+}
+
 // ---------------------------------------------------------------- engines ---
 
 constexpr int kBN = BN;
@@ -284,8 +321,7 @@ int launch_bwd_pair(const CUtensorMap* maps, const BwdParams& p, int sms, cudaSt
   if (int rc = ensure_smem_attr(kern, smem, done)) return rc;
   const int pairs = max_pairs(kern, smem, sms, pairs_cache, P_THREADS);
   timing_mark(1, 0, st);
-  const int rc =
-      launch_ex(kern, 2 * pairs, P_THREADS, smem, 2, st, maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], p);
+  const int rc = launch_ex(kern, 2 * pairs, P_THREADS, smem, 2, st, maps[0], maps[1], maps[2], maps[3], p);
   timing_mark(1, 1, st);
   return rc;
 }
@@ -818,21 +854,20 @@ int backward_impl(const void* hidden, const void* weight, const int64_t* labels,
   // buffers are one tensor: for the CTA-pair kernel G^T [NUM_GBUF * v_chunk, rows_pad]
   // (buffer b starts at vocab row b * v_chunk), for the one-CTA kernel G
   // [NUM_GBUF * rows_pad, v_chunk] (buffer b starts at token row b * rows_pad).
-  CUtensorMap maps[6];
+  CUtensorMap maps[7];
   const int g_rows = NUM_GBUF * L.rows_pad;
   const int gt_rows = NUM_GBUF * L.v_chunk;
   const bool pair = use_pair_backward(h);
   const bool mn3_h = h % 64 == 0 && h >= kBN;
   if (pair) {
-    // W K-major, W MN-major, X K-major, X MN-major, G^T K-major (over tokens), G^T MN-major
-    // (over tokens); every box is one CTA's half of a pair tile (128 rows, or two 64-column
-    // MN blocks)
-    if (int rc = make_map(&maps[0], weight, bf16, h, vl, h, BM)) return rc;
-    if (int rc = make_map_mn3(&maps[1], weight, bf16, h, vl, h, BM / 64)) return rc;
-    if (int rc = make_map(&maps[2], x_lab, bf16, h, L.rows_pad, h, BM)) return rc;
-    if (int rc = make_map_mn3(&maps[3], x_lab, bf16, h, L.rows_pad, h, BM / 64)) return rc;
-    if (int rc = make_map(&maps[4], g, bf16, L.rows_pad, gt_rows, L.rows_pad, BM)) return rc;
-    if (int rc = make_map_mn3(&maps[5], g, bf16, L.rows_pad, gt_rows, L.rows_pad, BM / 64)) return rc;
+    // W [V][H], X_lab [rows_pad][H] and G^T [NUM_GBUF * v_chunk][rows_pad], each as a 3-D view
+    // {64 elements, rows, 64-element blocks} with box {64, 128, 2}: one box is a CTA's share of
+    // a stage, K-major (128 rows x two k-blocks) or MN-major (128 k-rows x two MN blocks) alike
+    if (int rc = make_map_3d(&maps[0], weight, bf16, h, vl, h, 128, 2)) return rc;
+    if (int rc = make_map_3d(&maps[1], x_lab, bf16, h, L.rows_pad, h, 128, 2)) return rc;
+    if (int rc = make_map_3d(&maps[2], g, bf16, L.rows_pad, gt_rows, L.rows_pad, 128, 2)) return rc;
+    // the fp32 dX^T accumulator [H][rows_pad], 32 x 32 boxes for the epilogue's TMA stores and adds
+    if (int rc = make_map_f32(&maps[3], dx_acc, L.rows_pad, h, L.rows_pad, 32, 32)) return rc;
   } else {
     // x K-major, x MN-major, W K-major, W MN-major, G K-major, G MN-major (X and W fall
     // back to 2-D MN-major maps when H is below 256)
@@ -879,7 +914,6 @@ int backward_impl(const void* hidden, const void* weight, const int64_t* labels,
     p.x_hi = groups * (xch->rank + 1) / xch->world * 8;
   }
   p.dw_out = d_weight;
-  p.w = weight;
   p.want_dx = want_dx ? 1 : 0;
   p.want_dw = want_dw ? 1 : 0;
   p.mn3_h = mn3_h ? 1 : 0;
