@@ -312,6 +312,17 @@ LMCE_API int lmce_set_timing_events(int which, void* begin, void* end);
 LMCE_API int lmce_profile_read(void* counters, size_t counter_bytes, void* timeline, size_t timeline_bytes,
                                int reset);
 
+/* Measures the rate at which TMA loads reach the SMs; no counterpart in the reference. One
+ * CTA per SM streams `iters` stages of 32 KB from `tensor` (a caller-owned 16-bit
+ * [rows, cols] array, both multiples of 128; a few tens of MB keeps it in L2) and frees each
+ * stage as soon as it lands. box_kind 0: two 2-D {64, 128} boxes per stage (128 bytes of
+ * each of 128 rows); box_kind 1: one 3-D {64, 128, 2} box (256 contiguous bytes of each of
+ * 128 rows), the boxes the kernels load. cycles[sm] receives the SM clock cycles of the
+ * last iters - 9 stages, so bytes per clock per SM = (iters - 9) * 32768 / cycles[sm].
+ * Allocates nothing; n_cycles must be at least the number of SMs. */
+LMCE_API int lmce_probe_tma_rate(const void* tensor, int64_t rows, int64_t cols, int box_kind, int iters,
+                                 unsigned long long* cycles, int64_t n_cycles, void* stream);
+
 /* Launches a kernel whose bounded wait is never satisfied; after timeout_ns it
  * records LMCE_ERR_TIMEOUT in the device error word and returns normally.
  * Exercises the failure path without hanging or faulting the GPU. */

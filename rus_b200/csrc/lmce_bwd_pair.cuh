@@ -47,7 +47,6 @@ constexpr int P_EPI = 256;
 constexpr int P_A_BYTES = BM * P_KB * 2;                   // 128 rows x 128 k: 32 KB
 constexpr int P_B_BYTES = BM * P_KB * 2;                   // up to 128 rows (N / 2) x 128 k: 32 KB
 constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;       // 64 KB
-constexpr int P_BLOCK_BYTES = BM * BK * 2;                 // one 64-element block of a 128-row operand: 16 KB
 constexpr int P_RB = 256;                                  // token rows per row block
 // One epilogue warp's staging slice: a 32 x 32 fp32 block in the 128-byte swizzled layout
 // of a TMA box (4 KB, 1024-byte aligned), also used for 16-bit row staging and transposes.
@@ -185,16 +184,6 @@ struct PairCursor {
     }
   }
 };
-
-// Descriptor of UMMA k-step k (0..7, K = 16 each) of a 128-row operand staged by one
-// {64, 128, 2} box. K-major: two 16 KB blocks of 128 rows x 64 k (rows 128 bytes apart,
-// SBO 1024 per 8 rows), k-step k in block k / 4 at 32 bytes per step. MN-major: two
-// 64-element MN blocks 16 KB apart (LBO) of 128 k-rows of 128 bytes (SBO 1024 per 8
-// k-rows), k-step k at 16 k-rows = 2048 bytes per step.
-__device__ __forceinline__ uint64_t pair_operand_desc(uint32_t base, bool mn_major, int k) {
-  return mn_major ? smem_desc_sw128(base + k * (UMMA_K * 128), P_BLOCK_BYTES, 1024)
-                  : smem_desc_sw128(base + (k >> 2) * P_BLOCK_BYTES + (k & 3) * (UMMA_K * 2), 16, 1024);
-}
 
 // Pair UMMA k-loop of one tile (leader only); the instruction descriptor is a template
 // constant (see mma_tile). Both CTAs' empty barriers are signalled per stage.

@@ -278,15 +278,19 @@ int launch_stats(const CUtensorMap& mx, const CUtensorMap& mw, const StatsParams
   return rc;
 }
 
-// Pair kernels are used when a 256-row tile wastes no more rows than a 128-row one.
-// LMCE_TILE_MODE (compile time): 0 = that rule, 1 = always single CTA, 2 = pairs where possible.
+// Statistics on CTA pairs for more than 128 tokens unless 256-row tiles add more than a
+// quarter to the padded rows of 128-row ones: a pair's stage loads (one 256-byte-row box per
+// operand, 64 bytes per clock of UMMA work at full rate) stay within what TMA delivers to an
+// SM (~63 B/clk measured), a one-CTA 128 x 256 tile needs 96 B/clk and runs at ~2/3 of the
+// tensor rate. LMCE_TILE_MODE (compile time): 0 = that rule, 1 = always single CTA, 2 = pairs
+// where possible.
 #ifndef LMCE_TILE_MODE
 #define LMCE_TILE_MODE 0
 #endif
 bool use_pair_tiles(int64_t rows) {
   if (LMCE_TILE_MODE == 1) return false;
   if (LMCE_TILE_MODE == 2) return rows > BM;
-  return rows > BM && ((rows + 255) / 256) * 256 <= ((rows + 127) / 128) * 128;
+  return rows > BM && ((rows + 255) / 256) * 256 * 4 <= ((rows + 127) / 128) * 128 * 5;
 }
 
 // Units that can run at once for the statistics kernel (CTAs, or pairs of CTAs).
@@ -607,6 +611,79 @@ __global__ void selftest_wait_kernel(unsigned long long timeout_ns, int* err) {
   __syncthreads();
 }
 
+// TMA load rate probe (diagnostic): one CTA per SM streams `iters` stages of 32 KB from a
+// tensor through a ring of three stages and frees each stage as soon as it lands, so only
+// the rate at which TMA delivers bytes to the SM is measured. kind 0: two 2-D {64, 128}
+// boxes per stage (128 bytes of each row); kind 1: one 3-D {64, 128, 2} box (256 contiguous
+// bytes of each row), the boxes the kernels load. Every wait is bounded.
+constexpr int PROBE_STAGES = 3;
+constexpr int PROBE_STAGE_BYTES = 32768;
+__global__ void __launch_bounds__(64, 1) tma_rate_probe_kernel(const __grid_constant__ CUtensorMap map2,
+                                                               const __grid_constant__ CUtensorMap map3, int kind,
+                                                               int iters, int row_blocks, int kblocks,
+                                                               unsigned long long timeout_ns,
+                                                               unsigned long long* cycles, int* err) {
+  extern __shared__ uint8_t raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + PROBE_STAGES * PROBE_STAGE_BYTES);
+  uint64_t* empty = full + PROBE_STAGES;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < PROBE_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int i = 0; i < iters; ++i) {
+      if (!mbar_wait(&empty[stage], phase ^ 1u, &abort_flag, timeout_ns)) {
+        raise_error(err, ERR_TIMEOUT);
+        abort_flag = 1;
+        break;
+      }
+      mbar_arrive_expect_tx(&full[stage], PROBE_STAGE_BYTES);
+      const int blk = (blockIdx.x * 37 + i / kblocks) % row_blocks;  // 128-row block
+      const int kb = (i % kblocks) & ~1;                              // pair of 64-element blocks
+      uint8_t* dst = smem + stage * PROBE_STAGE_BYTES;
+      if (kind == 0) {
+        tma_load_2d(dst, &map2, &full[stage], kb * 64, blk * 128);
+        tma_load_2d(dst + 16384, &map2, &full[stage], kb * 64 + 64, blk * 128);
+      } else {
+        tma_load_3d(dst, &map3, &full[stage], 0, blk * 128, kb);
+      }
+      if (++stage == PROBE_STAGES) {
+        stage = 0;
+        phase ^= 1u;
+      }
+    }
+  } else if (threadIdx.x == 32) {
+    int stage = 0;
+    uint32_t phase = 0;
+    long long t0 = 0, t1 = 0;
+    for (int i = 0; i < iters; ++i) {
+      if (!mbar_wait(&full[stage], phase, &abort_flag, timeout_ns)) {
+        raise_error(err, ERR_TIMEOUT);
+        abort_flag = 1;
+        break;
+      }
+      if (i == 8) t0 = clock64();
+      if (i == iters - 1) t1 = clock64();
+      mbar_arrive(&empty[stage]);
+      if (++stage == PROBE_STAGES) {
+        stage = 0;
+        phase ^= 1u;
+      }
+    }
+    cycles[blockIdx.x] = static_cast<unsigned long long>(t1 - t0);
+  }
+  __syncthreads();
+}
+
 // ------------------------------------------------------------ workspace ---
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -727,8 +804,13 @@ int lmce_fwd_stats(const void* hidden, const void* weight, const int64_t* labels
   if (n_parts < 1 || n_parts > num_n) return fail(LMCE_ERR_INVALID_ARGUMENT, "n_parts %lld out of range", (long long)n_parts);
   const bool bf16 = dtype == LMCE_DTYPE_BF16;
   CUtensorMap mx, mw;
-  if (int rc = make_map(&mx, hidden, bf16, hidden_dim, n_tokens, hidden_dim, BM)) return rc;
-  if (int rc = make_map(&mw, weight, bf16, hidden_dim, vocab_local, hidden_dim, pair ? kBN / 2 : kBN)) return rc;
+  if (pair) {  // 3-D views, box {64, 128, 2}: a CTA's 128 rows x two k-blocks per stage
+    if (int rc = make_map_3d(&mx, hidden, bf16, hidden_dim, n_tokens, hidden_dim, 128, 2)) return rc;
+    if (int rc = make_map_3d(&mw, weight, bf16, hidden_dim, vocab_local, hidden_dim, 128, 2)) return rc;
+  } else {
+    if (int rc = make_map(&mx, hidden, bf16, hidden_dim, n_tokens, hidden_dim, BM)) return rc;
+    if (int rc = make_map(&mw, weight, bf16, hidden_dim, vocab_local, hidden_dim, kBN)) return rc;
+  }
   StatsParams p{};
   p.M = static_cast<int>(n_tokens);
   p.N = static_cast<int>(vocab_local);
@@ -1167,6 +1249,30 @@ int lmce_selftest_wait_timeout(uint64_t timeout_ns, void* stream) {
 }
 
 uint64_t lmce_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int lmce_probe_tma_rate(const void* tensor, int64_t rows, int64_t cols, int box_kind, int iters,
+                        unsigned long long* cycles, int64_t n_cycles, void* stream) {
+  if (!tensor || !cycles) return fail(LMCE_ERR_INVALID_ARGUMENT, "null pointer");
+  if (rows < 128 || rows % 128 != 0 || cols < 128 || cols % 128 != 0)
+    return fail(LMCE_ERR_INVALID_ARGUMENT, "rows and cols must be positive multiples of 128");
+  if (box_kind != 0 && box_kind != 1) return fail(LMCE_ERR_INVALID_ARGUMENT, "box_kind must be 0 or 1");
+  if (iters < 16) return fail(LMCE_ERR_INVALID_ARGUMENT, "iters must be at least 16");
+  DevInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+  if (n_cycles < d->sms) return fail(LMCE_ERR_INVALID_ARGUMENT, "cycles needs one entry per SM (%d)", d->sms);
+  if (int rc = get_encoder()) return rc;
+  CUtensorMap m2, m3;
+  if (int rc = make_map(&m2, tensor, false, cols, rows, cols, 128)) return rc;
+  if (int rc = make_map_3d(&m3, tensor, false, cols, rows, cols, 128, 2)) return rc;
+  auto kern = tma_rate_probe_kernel;
+  const int smem = PROBE_STAGES * PROBE_STAGE_BYTES + 2048;
+  static bool done[kMaxDevices] = {};
+  if (int rc = ensure_smem_attr(kern, smem, done)) return rc;
+  kern<<<d->sms, 64, smem, static_cast<cudaStream_t>(stream)>>>(m2, m3, box_kind, iters, static_cast<int>(rows / 128),
+                                                              static_cast<int>(cols / 64), wait_timeout_ns(), cycles,
+                                                              d->err_ptr);
+  return launched();
+}
 
 int lmce_profile_read(void* counters, size_t counter_bytes, void* timeline, size_t timeline_bytes, int reset) {
 #if LMCE_ROLE_PROFILE

@@ -34,17 +34,20 @@ constexpr float NEG_BIG = -1.0e30f;  // finite "minus infinity" for running maxi
 constexpr int MN_BOX_BYTES = 64 * BK * 2;     // one {64 MN, 64 K} TMA box of an MN-major operand
 
 // Tile geometry. Single CTA: a 128 x 256 output tile, the CTA holds 128 A rows and
-// 256 B rows per k-block (48 KB stages, 4 of them). Pair (cta_group::2): a 256 x 256
-// output tile over two CTAs; each CTA holds 128 A rows and 128 B rows per k-block
-// (32 KB stages, 6 of them) and 128 accumulator lanes; the leader issues the UMMAs.
+// 256 B rows per k-block of 64 (48 KB stages, 4 of them). Pair (cta_group::2): a 256 x 256
+// output tile over two CTAs; each CTA holds 128 A rows and 128 B rows of K = 128 per stage
+// (64 KB stages, 3 of them), each operand loaded as one {64, 128, 2} box of a 3-D view
+// (256 contiguous bytes per row; see pair_operand_desc), and 128 accumulator lanes; the
+// leader issues the UMMAs.
 template <bool PAIR>
 struct TileCfg {
   static constexpr int TILE_M = PAIR ? 2 * BM : BM;     // output rows per tile
   static constexpr int B_ROWS = PAIR ? BN / 2 : BN;     // B rows staged by one CTA
-  static constexpr int A_BYTES = BM * BK * 2;           // 16 KB
-  static constexpr int B_BYTES = B_ROWS * BK * 2;       // 16 or 32 KB
+  static constexpr int KB = PAIR ? 2 * BK : BK;         // K per stage
+  static constexpr int A_BYTES = BM * KB * 2;           // 16 KB (one CTA) or 32 KB (pair)
+  static constexpr int B_BYTES = B_ROWS * KB * 2;       // 32 KB
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = PAIR ? 6 : 4;
+  static constexpr int STAGES = PAIR ? 3 : 4;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align slack*/ + 1024 /*barriers, ring*/;
   static constexpr int CTAS = PAIR ? 2 : 1;
 };
@@ -168,6 +171,17 @@ __device__ __forceinline__ void load_operand_mn3(uint8_t* dst, const CUtensorMap
   tma_load_3d(dst, map, bar, 0, k0, row0 / 64);
 }
 
+// Descriptor of UMMA k-step k (0..7, K = 16 each) of a 128-row operand staged by one
+// {64, 128, 2} box: K = 128 per stage. K-major: two 16 KB blocks of 128 rows x 64 k (rows
+// 128 bytes apart, SBO 1024 per 8 rows), k-step k in block k / 4 at 32 bytes per step.
+// MN-major: two 64-element MN blocks 16 KB apart (LBO) of 128 k-rows of 128 bytes (SBO 1024
+// per 8 k-rows), k-step k at 16 k-rows = 2048 bytes per step.
+constexpr int BLOCK128_BYTES = BM * BK * 2;  // one 64-element block of a 128-row operand: 16 KB
+__device__ __forceinline__ uint64_t pair_operand_desc(uint32_t base, bool mn_major, int k) {
+  return mn_major ? smem_desc_sw128(base + k * (UMMA_K * 128), BLOCK128_BYTES, 1024)
+                  : smem_desc_sw128(base + (k >> 2) * BLOCK128_BYTES + (k & 3) * (UMMA_K * 2), 16, 1024);
+}
+
 // Descriptor of UMMA k-step k (K = 16) inside a staged operand. K-major: rows of
 // 128 bytes in 8-row swizzle atoms (SBO 1024), k advances 32 bytes within the row.
 // MN-major: K rows of 128 bytes (8-row groups, SBO 1024), 64-wide MN blocks
@@ -185,10 +199,10 @@ __device__ __forceinline__ uint64_t operand_desc(uint32_t base, bool mn_major, i
 // statistics each epilogue thread carries in registers.
 struct StatsSchedule {
   int num_m, num_n, n_slabs, total, num_kb;
-  __device__ __forceinline__ void init(const StatsParams& p, int tile_m) {
+  __device__ __forceinline__ void init(const StatsParams& p, int tile_m, int kb) {
     num_m = (p.M + tile_m - 1) / tile_m;
     num_n = (p.N + BN - 1) / BN;
-    num_kb = (p.K + BK - 1) / BK;
+    num_kb = (p.K + kb - 1) / kb;
     n_slabs = p.n_slabs;
     total = num_m * n_slabs;
   }
@@ -223,7 +237,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int unit_step = PAIR ? static_cast<int>(cluster_count_x()) : static_cast<int>(gridDim.x);
 
   StatsSchedule sch;
-  sch.init(p, C::TILE_M);
+  sch.init(p, C::TILE_M, C::KB);
   if (unit0 >= sch.total) return;  // uniform for the CTA (and for both CTAs of a pair)
 
   if (threadIdx.x == 0) {
@@ -277,13 +291,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
             uint8_t* sa = smem + stage * C::STAGE_BYTES;
             uint8_t* sb = sa + C::A_BYTES;
-            const int k0 = kb * BK;
+            const int k0 = kb * C::KB;
             if constexpr (PAIR) {
-              // both CTAs' copies count on the leader's full barrier
+              // both CTAs' copies count on the leader's full barrier; one {64, 128, 2} box per
+              // operand: this CTA's 128 rows x two k-blocks
               if (rank == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * C::STAGE_BYTES);
               const uint32_t fb = mapa_shared(smem_u32(&full_bar[stage]), 0);
-              tma_load_2d_pair(sa, &map_x, fb, k0, m_blk * C::TILE_M + BM * static_cast<int>(rank));
-              tma_load_2d_pair(sb, &map_w, fb, k0, n_blk * BN + C::B_ROWS * static_cast<int>(rank));
+              tma_load_3d_pair(sa, &map_x, fb, 0, m_blk * C::TILE_M + BM * static_cast<int>(rank), 2 * kb);
+              tma_load_3d_pair(sb, &map_w, fb, 0, n_blk * BN + C::B_ROWS * static_cast<int>(rank), 2 * kb);
             } else {
               mbar_arrive_expect_tx(&full_bar[stage], C::STAGE_BYTES);
               load_operand<BM>(sa, &map_x, &full_bar[stage], false, m_blk * BM, k0);
@@ -345,12 +360,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             tc_fence_after();
             const uint32_t sa = smem_u32(smem + stage * C::STAGE_BYTES);
 #pragma unroll
-            for (int k = 0; k < BK / UMMA_K; ++k) {
-              const uint64_t da = operand_desc(sa, false, k), db = operand_desc(sa + C::A_BYTES, false, k);
+            for (int k = 0; k < C::KB / UMMA_K; ++k) {
               if constexpr (PAIR)
-                umma_f16_ss_pair(d_tmem, da, db, idesc, (kb | k) != 0 ? 1u : 0u);
+                umma_f16_ss_pair(d_tmem, pair_operand_desc(sa, false, k), pair_operand_desc(sa + C::A_BYTES, false, k),
+                                 idesc, (kb | k) != 0 ? 1u : 0u);
               else
-                umma_f16_ss(d_tmem, da, db, idesc, (kb | k) != 0 ? 1u : 0u);
+                umma_f16_ss(d_tmem, operand_desc(sa, false, k), operand_desc(sa + C::A_BYTES, false, k), idesc,
+                            (kb | k) != 0 ? 1u : 0u);
             }
             if constexpr (PAIR) {
               umma_commit_pair(smem_u32(&empty_bar[stage]));
