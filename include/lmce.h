@@ -110,9 +110,10 @@ LMCE_API int lmce_stats_finish(const lmce_part* parts, int64_t n_parts, int64_t 
 
 /* Workspace bytes for lmce_backward (vocab-chunk gradient tiles, compacted
  * rows, fp32 dX accumulator). v_chunk is rounded up to a multiple of 256;
- * v_chunk <= 0 selects the default: gradient buffers of about 160 MiB within
- * 8192..20480 vocab rows for the CTA-pair kernel (hidden_dim >= 256), about
- * 64 MiB within 8192..32768 rows for the one-CTA kernel. */
+ * v_chunk <= 0 selects the default: gradient buffers of about 90 MiB within
+ * 4096..20480 vocab rows for the CTA-pair kernel (hidden_dim >= 256), about
+ * 64 MiB within 8192..32768 rows for the one-CTA kernel; either way at most
+ * half the bytes of an [n_tokens, vocab_local] logits buffer. */
 LMCE_API size_t lmce_bwd_workspace_bytes(int64_t n_tokens, int64_t hidden_dim, int64_t vocab_local, int64_t v_chunk);
 
 /* Recomputes the logits per vocab chunk, forms G = (softmax - onehot) in

@@ -693,21 +693,25 @@ struct BwdLayout {
   int rows_pad, v_chunk, n_chunks, sync_ints;
 };
 
-// Default vocab chunk of the backward. Few tokens per chunk leave the dX chain and
-// the per-chunk dependencies exposed, so small N prefers wide chunks; large N prefers
-// narrower ones to bound the G buffers (three of N x v_chunk). Measured on one B200:
-// the pair kernel does best with G buffers of about 160 MiB and chunks of at most
-// 20480 rows, the one-CTA kernel with about 64 MiB and at most 32768 rows. For few
-// tokens the chunk is also capped so that the G buffers stay at most half the size of
-// an [N, V] logits buffer: with the 256-row padding of the [rows, H] buffers the whole
-// workspace stays below [N, V] in the input dtype for every N >= 64.
+// Default vocab chunk of the backward. CTA-pair kernel: gradient buffers (three of
+// rows_pad x v_chunk) of about 90 MiB, within 4096..20480 vocab rows; measured on one B200
+// at config 2 under sustained load, 8192-row chunks run within 0.3% of 20480-row ones (the
+// K = 128 stages keep the UMMA fed at every chunk width), so the memory-lean size is the
+// default. One-CTA kernel: about 64 MiB within 8192..32768 rows. For few tokens the chunk
+// is also capped so that the G buffers stay at most half the size of an [N, V] logits
+// buffer: with the 256-row padding of the [rows, H] buffers the whole workspace stays
+// below [N, V] in the input dtype for every N >= 64.
 int64_t auto_v_chunk(int64_t n, int64_t rows_pad, int64_t v_local, bool pair) {
-  const int64_t budget = pair ? (160ll << 20) : (64ll << 20);
-  int64_t vc = budget / (2 * rows_pad);
-  vc = vc / 2048 * 2048;
-  if (vc < 8192) vc = 8192;
-  const int64_t vmax = pair ? 20480 : 32768;
-  if (vc > vmax) vc = vmax;
+  int64_t vc;
+  if (pair) {
+    vc = (90ll << 20) / (2 * NUM_GBUF * rows_pad) / 256 * 256;
+    if (vc < 4096) vc = 4096;
+    if (vc > 20480) vc = 20480;
+  } else {
+    vc = (64ll << 20) / (2 * rows_pad) / 2048 * 2048;
+    if (vc < 8192) vc = 8192;
+    if (vc > 32768) vc = 32768;
+  }
   const int64_t g_rows = NUM_GBUF * ((n + 255) / 256 * 256);
   const int64_t cap = (n * v_local / 2) / g_rows / 256 * 256;  // G bytes <= n * v_local bytes
   if (vc > cap) vc = cap < 256 ? 256 : cap;

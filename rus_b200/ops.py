@@ -275,7 +275,7 @@ def chunked_lm_head(hidden_states, shift_labels, weight_or_host_head, num_items_
     """Drop-in for ``solution.ops.chunked_lm_head`` (ops.py:342-349).
 
     ``v_chunk`` is the vocab chunk of the gradient pass; ``None`` (the default) lets the
-    library size it (for the CTA-pair kernel gradient buffers of ~160 MiB, at most 20480
+    library size it (for the CTA-pair kernel gradient buffers of ~90 MiB, 4096..20480
     vocab rows); an explicit value is used as given. ``tied_slot`` (a
     ``rus_b200.tied.TiedGradSlot`` shared with ``tied_embedding``) hands dW to the tied
     input embedding's backward, which adds its own gradient into the same buffer."""
