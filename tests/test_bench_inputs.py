@@ -1,0 +1,48 @@
+"""CPU: the benchmark's seeded config generators (bench.make_config) follow the configs of
+shapes, dtypes, row-length laws, label masks and the planted argmax ties."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import bench
+
+
+@pytest.mark.parametrize("cfg", ["c1", "c2", "c5"])
+def test_config_shapes_and_masks(cfg):
+    H, V, dt, _ = bench.CONFIGS[cfg]
+    X, y, W, lens = bench.make_config(cfg, "cpu")
+    n = sum(lens)
+    assert X.shape == (n, H) and X.dtype == dt and W.shape == (V, H) and W.dtype == dt and y.shape == (n,)
+    assert int(y[y != -100].min()) >= 0 and int(y.max()) < V
+    starts = np.concatenate([[0], np.cumsum(lens)[:-1]])
+    if cfg == "c1":
+        assert len(lens) == 4 and all(16 <= L <= 512 for L in lens)
+        for s0, L in zip(starts, lens):  # first 40% of each row ignored, the rest labelled
+            k = int(0.4 * L)
+            assert (y[s0:s0 + k] == -100).all() and (y[s0 + k:s0 + L] != -100).all()
+    elif cfg == "c2":
+        assert lens == [512] * 4
+        frac = float((y == -100).float().mean())
+        assert 0.07 < frac < 0.13
+    else:  # c5: Zipf(1.2) lengths truncated to 1..512, three rows all ignored, planted ties
+        assert len(lens) == 64 and all(1 <= L <= 512 for L in lens) and 1500 <= n <= 4500
+        full = sum(bool((y[s0:s0 + L] == -100).all()) for s0, L in zip(starts, lens))
+        assert full >= 3
+        assert len(torch.unique(W, dim=0)) < V
+
+
+def test_weak_scaling_replicas_stack_independent_batches():
+    X1, y1, W1, l1 = bench.make_config("c2", "cpu", replicas=1)
+    X2, y2, W2, l2 = bench.make_config("c2", "cpu", replicas=2)
+    assert X2.shape[0] == 2 * X1.shape[0] and torch.equal(W1, W2)
+    assert torch.equal(X2[: X1.shape[0]], X1) and not torch.equal(X2[X1.shape[0]:], X1)
+
+
+def test_peak_choice_follows_the_clock_record():
+    peaks = {"bf16_tflops": 1635.7, "bf16_tflops_sustained": 1396.7}
+    burst = bench.choose_peak(peaks, {"sm_mhz": 1965.0, "sm_max_mhz": 1965.0, "power_capped_fraction": 0.0})
+    capped = bench.choose_peak(peaks, {"sm_mhz": 1350.0, "sm_max_mhz": 1965.0, "power_capped_fraction": 0.9})
+    assert burst[0] == 1635.7 and "burst" in burst[1]
+    assert capped[0] == 1396.7 and "sustained" in capped[1]
