@@ -347,10 +347,12 @@ def main():
             return sharded_lm_head(xx, yy, W, v_lo, V, group, None, args.v_chunk)
         return chunked_lm_head(xx, yy, W, None, args.v_chunk)
 
-    def step():
+    def step(mid=None):
         Xg.grad = None
         W.grad = None
         loss, nll, ent, arg = head(Xg, y)
+        if mid is not None:
+            mid.record(stream)  # between the forward and the backward phase
         loss.backward()
         return loss
 
@@ -440,6 +442,7 @@ def main():
     stage("timed steps")
     l0 = _lib.launch_count()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    ev_mid = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     kev = {k: [(new_event(), new_event()) for _ in range(args.steps)] for k in (0, 1)}
     e2e_a = torch.cuda.Event(enable_timing=True)
     e2e_b = torch.cuda.Event(enable_timing=True)
@@ -450,7 +453,7 @@ def main():
             for k in (0, 1):
                 _lib.call("lmce_set_timing_events", k, kev[k][i][0].cuda_event, kev[k][i][1].cuda_event)
             ev[i][0].record(stream)
-            step()
+            step(ev_mid[i])
             ev[i][1].record(stream)
         for k in (0, 1):
             _lib.call("lmce_set_timing_events", k, None, None)
@@ -475,6 +478,9 @@ def main():
         launches += _lib.launch_count() - l1
     step_ms = [a.elapsed_time(b) for a, b in ev]
     kern_ms = {k: statistics.mean(a.elapsed_time(b) for a, b in kev[k]) for k in (0, 1)}
+    # forward phase (statistics kernel, record merge / exchange, finish, loss) and backward phase
+    fwd_phase_ms = statistics.mean(a.elapsed_time(m) for (a, _), m in zip(ev, ev_mid))
+    bwd_phase_ms = statistics.mean(m.elapsed_time(b) for (_, b), m in zip(ev, ev_mid))
     total_ms = torch.tensor([sum(step_ms)], dtype=torch.float64, device=device)
     e2e_ms = torch.tensor([e2e_a.elapsed_time(e2e_b)], dtype=torch.float64, device=device)
     if world > 1:
@@ -588,6 +594,9 @@ def main():
                 "step_frac": step_tflops / k_peak,
             },
             "kernels": {k: {kk: v for kk, v in d.items() if kk != "name"} for k, d in kernels.items()},
+            "phases_ms": {"forward": fwd_phase_ms, "backward": bwd_phase_ms,
+                          "forward_outside_stats_kernel": fwd_phase_ms - kern_ms[0],
+                          "backward_outside_backward_kernel": bwd_phase_ms - kern_ms[1]},
             "clocks": clocks,
             "device_error": err,
         }
