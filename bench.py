@@ -347,13 +347,20 @@ def main():
             return sharded_lm_head(xx, yy, W, v_lo, V, group, None, args.v_chunk)
         return chunked_lm_head(xx, yy, W, None, args.v_chunk)
 
+    host_s = [0.0, 0.0]  # host time spent issuing the forward / the backward of the timed steps
+
     def step(mid=None):
         Xg.grad = None
         W.grad = None
+        h0 = time.perf_counter()
         loss, nll, ent, arg = head(Xg, y)
         if mid is not None:
             mid.record(stream)  # between the forward and the backward phase
+        h1 = time.perf_counter()
         loss.backward()
+        if mid is not None:
+            host_s[0] += h1 - h0
+            host_s[1] += time.perf_counter() - h1
         return loss
 
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
@@ -529,7 +536,19 @@ def main():
     step_flops = 2.0 * n_tokens * H * v_local + 4.0 * n_lab * H * v_local
     step_tflops = step_flops / (ms_per_step / 1e3) / 1e12
 
+    # per-rank view (N > 1): every rank's mean step, kernel and phase times and its median SM
+    # clock, so that rank-to-rank speed differences (which the max over ranks absorbs) show
+    per_rank = None
     if world > 1:
+        mine = torch.tensor([statistics.mean(step_ms), kern_ms[0], kern_ms[1], fwd_phase_ms, bwd_phase_ms,
+                             float(clocks.get("sm_mhz") or 0.0), 1e3 * host_s[0] / args.steps,
+                             1e3 * host_s[1] / args.steps], dtype=torch.float64, device=device)
+        allr = torch.empty((world, mine.numel()), dtype=torch.float64, device=device)
+        dist.all_gather_into_tensor(allr, mine)
+        cols = allr.t().tolist()
+        per_rank = {k: [round(v, 4) for v in c] for k, c in
+                    zip(("step_ms", "stats_ms", "backward_ms", "forward_phase_ms", "backward_phase_ms",
+                         "sm_mhz", "host_forward_ms", "host_backward_ms"), cols)}
         dist.barrier(device_ids=[local_rank])
     err = _lib.device_error(reset=True)
     if err:
@@ -594,12 +613,15 @@ def main():
                 "step_frac": step_tflops / k_peak,
             },
             "kernels": {k: {kk: v for kk, v in d.items() if kk != "name"} for k, d in kernels.items()},
+            "host_issue_ms": {"forward": 1e3 * host_s[0] / args.steps, "backward": 1e3 * host_s[1] / args.steps},
             "phases_ms": {"forward": fwd_phase_ms, "backward": bwd_phase_ms,
                           "forward_outside_stats_kernel": fwd_phase_ms - kern_ms[0],
                           "backward_outside_backward_kernel": bwd_phase_ms - kern_ms[1]},
             "clocks": clocks,
             "device_error": err,
         }
+        if per_rank is not None:
+            line["per_rank"] = per_rank
         if cpu_base is not None:
             line["cpu_baseline"] = cpu_base
         print(json.dumps(line), flush=True)

@@ -313,14 +313,26 @@ LMCE_API int lmce_set_timing_events(int which, void* begin, void* end);
 LMCE_API int lmce_profile_read(void* counters, size_t counter_bytes, void* timeline, size_t timeline_bytes,
                                int reset);
 
-/* Measures the rate at which TMA loads reach the SMs; no counterpart in the reference. One
- * CTA per SM streams `iters` stages of 32 KB from `tensor` (a caller-owned 16-bit
- * [rows, cols] array, both multiples of 128; a few tens of MB keeps it in L2) and frees each
- * stage as soon as it lands. box_kind 0: two 2-D {64, 128} boxes per stage (128 bytes of
- * each of 128 rows); box_kind 1: one 3-D {64, 128, 2} box (256 contiguous bytes of each of
- * 128 rows), the boxes the kernels load. cycles[sm] receives the SM clock cycles of the
- * last iters - 9 stages, so bytes per clock per SM = (iters - 9) * 32768 / cycles[sm].
- * Allocates nothing; n_cycles must be at least the number of SMs. */
+/* Measures how fast TMA loads reach the SMs through a ring of stages; no counterpart in the
+ * reference. One CTA per SM streams `iters` stages of `stage_bytes` from `tensor` (a
+ * caller-owned 16-bit [rows, cols] array, both multiples of 128, 16-byte aligned; a few tens
+ * of MB stays in L2, a few hundred MB comes from DRAM) through a ring of `stages` stages
+ * (2..8, stages x stage_bytes + 2 KB within 226 KB): one thread loads each stage as soon as
+ * it is free, another holds each landed stage for `hold_cycles` SM cycles (a stand-in for the
+ * UMMAs that read it; 0 frees it at once) and frees it. load_kind 0: 2-D {64, 128} boxes (128
+ * bytes of each of 128 rows, 16 KB each); 1: 3-D {64, 128, 2} boxes (256 contiguous bytes of
+ * each of 128 rows, 32 KB each), the boxes the kernels load; 2: plain bulk copies of 32
+ * contiguous KB. stage_bytes must be a multiple of the piece size (16 KB for kind 0, 32 KB
+ * otherwise). cycles[sm] receives the SM clock cycles of the last iters - 9 stages, so bytes
+ * per clock per SM = (iters - 9) * stage_bytes / cycles[sm], and the share of time the
+ * holder was busy = (iters - 9) * hold_cycles / cycles[sm]. Allocates nothing; n_cycles must
+ * be at least the number of SMs. */
+LMCE_API int lmce_probe_tma_pipeline(const void* tensor, int64_t rows, int64_t cols, int load_kind,
+                                     int stage_bytes, int stages, int hold_cycles, int iters,
+                                     unsigned long long* cycles, int64_t n_cycles, void* stream);
+
+/* lmce_probe_tma_pipeline with three 32 KB stages freed at once; box_kind 0 or 1 as its
+ * load_kind. */
 LMCE_API int lmce_probe_tma_rate(const void* tensor, int64_t rows, int64_t cols, int box_kind, int iters,
                                  unsigned long long* cycles, int64_t n_cycles, void* stream);
 

@@ -95,6 +95,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "lmce_set_timing_events": (_int, [_int, _vp, _vp]),
     "lmce_profile_read": (_int, [_vp, ctypes.c_size_t, _vp, ctypes.c_size_t, _int]),
     "lmce_probe_tma_rate": (_int, [_vp, _i64, _i64, _int, _int, _vp, _i64, _vp]),
+    "lmce_probe_tma_pipeline": (_int, [_vp, _i64, _i64, _int, _int, _int, _int, _int, _vp, _i64, _vp]),
     "lmce_forward_noalloc": (
         _int,
         [_vp, _vp, _vp, _i64, _i64, _i64, _int, _vp, ctypes.c_double, _vp, _vp, _vp, _vp, _vp, _vp, _vp],

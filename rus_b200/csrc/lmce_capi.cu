@@ -611,25 +611,25 @@ __global__ void selftest_wait_kernel(unsigned long long timeout_ns, int* err) {
   __syncthreads();
 }
 
-// TMA load rate probe (diagnostic): one CTA per SM streams `iters` stages of 32 KB from a
-// tensor through a ring of three stages and frees each stage as soon as it lands, so only
-// the rate at which TMA delivers bytes to the SM is measured. kind 0: two 2-D {64, 128}
-// boxes per stage (128 bytes of each row); kind 1: one 3-D {64, 128, 2} box (256 contiguous
-// bytes of each row), the boxes the kernels load. Every wait is bounded.
-constexpr int PROBE_STAGES = 3;
-constexpr int PROBE_STAGE_BYTES = 32768;
-__global__ void __launch_bounds__(64, 1) tma_rate_probe_kernel(const __grid_constant__ CUtensorMap map2,
-                                                               const __grid_constant__ CUtensorMap map3, int kind,
-                                                               int iters, int row_blocks, int kblocks,
-                                                               unsigned long long timeout_ns,
-                                                               unsigned long long* cycles, int* err) {
+// TMA pipeline probe (diagnostic): one CTA per SM streams `iters` stages from a tensor through
+// a ring of `stages` stages of `stage_bytes`; one thread loads each stage as soon as it is
+// free, another waits for it, holds it `hold` cycles (a stand-in for the UMMAs that read a
+// stage) and frees it. kind 0: 2-D {64, 128} boxes (128 bytes of each of 128 rows, 16 KB);
+// kind 1: 3-D {64, 128, 2} boxes (256 contiguous bytes of each of 128 rows, 32 KB), the boxes
+// the kernels load; kind 2: plain bulk copies of 32 contiguous KB. Every wait is bounded.
+constexpr int PROBE_MAX_STAGES = 8;
+constexpr int PROBE_MAX_SMEM = 226 * 1024;  // dynamic, below the 227 KB opt-in limit
+__global__ void __launch_bounds__(64, 1) tma_pipeline_probe_kernel(
+    const __grid_constant__ CUtensorMap map2, const __grid_constant__ CUtensorMap map3, const uint8_t* base,
+    long long n_pieces32, int kind, int stage_bytes, int stages, int hold, int iters, int row_blocks, int kblocks,
+    unsigned long long timeout_ns, unsigned long long* cycles, int* err) {
   extern __shared__ uint8_t raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + PROBE_STAGES * PROBE_STAGE_BYTES);
-  uint64_t* empty = full + PROBE_STAGES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(stages) * stage_bytes);
+  uint64_t* empty = full + PROBE_MAX_STAGES;
   __shared__ int abort_flag;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < PROBE_STAGES; ++s) {
+    for (int s = 0; s < stages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -637,6 +637,8 @@ __global__ void __launch_bounds__(64, 1) tma_rate_probe_kernel(const __grid_cons
     fence_barrier_init();
   }
   __syncthreads();
+  const int piece = kind == 0 ? 16384 : 32768;
+  const int pieces = stage_bytes / piece;
   if (threadIdx.x == 0) {
     int stage = 0;
     uint32_t phase = 0;
@@ -646,17 +648,22 @@ __global__ void __launch_bounds__(64, 1) tma_rate_probe_kernel(const __grid_cons
         abort_flag = 1;
         break;
       }
-      mbar_arrive_expect_tx(&full[stage], PROBE_STAGE_BYTES);
-      const int blk = (blockIdx.x * 37 + i / kblocks) % row_blocks;  // 128-row block
-      const int kb = (i % kblocks) & ~1;                              // pair of 64-element blocks
-      uint8_t* dst = smem + stage * PROBE_STAGE_BYTES;
-      if (kind == 0) {
-        tma_load_2d(dst, &map2, &full[stage], kb * 64, blk * 128);
-        tma_load_2d(dst + 16384, &map2, &full[stage], kb * 64 + 64, blk * 128);
-      } else {
-        tma_load_3d(dst, &map3, &full[stage], 0, blk * 128, kb);
+      mbar_arrive_expect_tx(&full[stage], static_cast<uint32_t>(stage_bytes));
+      uint8_t* dst = smem + static_cast<size_t>(stage) * stage_bytes;
+      for (int q = 0; q < pieces; ++q) {
+        const long long u = static_cast<long long>(blockIdx.x) * 7919 + static_cast<long long>(i) * pieces + q;
+        if (kind == 0) {  // one 64-element block of one 128-row block
+          tma_load_2d(dst + q * piece, &map2, &full[stage], static_cast<int>(u % kblocks) * 64,
+                      static_cast<int>((u / kblocks) % row_blocks) * 128);
+        } else if (kind == 1) {  // two adjacent 64-element blocks of one 128-row block
+          const int kp = kblocks / 2;
+          tma_load_3d(dst + q * piece, &map3, &full[stage], 0, static_cast<int>((u / kp) % row_blocks) * 128,
+                      static_cast<int>(u % kp) * 2);
+        } else {
+          bulk_load(dst + q * piece, base + (u % n_pieces32) * 32768, 32768, &full[stage]);
+        }
       }
-      if (++stage == PROBE_STAGES) {
+      if (++stage == stages) {
         stage = 0;
         phase ^= 1u;
       }
@@ -671,10 +678,13 @@ __global__ void __launch_bounds__(64, 1) tma_rate_probe_kernel(const __grid_cons
         abort_flag = 1;
         break;
       }
-      if (i == 8) t0 = clock64();
+      const long long got = clock64();
+      if (i == 8) t0 = got;
+      while (clock64() - got < hold) {
+      }
       if (i == iters - 1) t1 = clock64();
       mbar_arrive(&empty[stage]);
-      if (++stage == PROBE_STAGES) {
+      if (++stage == stages) {
         stage = 0;
         phase ^= 1u;
       }
@@ -1254,12 +1264,22 @@ int lmce_selftest_wait_timeout(uint64_t timeout_ns, void* stream) {
 
 uint64_t lmce_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
-int lmce_probe_tma_rate(const void* tensor, int64_t rows, int64_t cols, int box_kind, int iters,
-                        unsigned long long* cycles, int64_t n_cycles, void* stream) {
+int lmce_probe_tma_pipeline(const void* tensor, int64_t rows, int64_t cols, int load_kind, int stage_bytes,
+                            int stages, int hold_cycles, int iters, unsigned long long* cycles, int64_t n_cycles,
+                            void* stream) {
   if (!tensor || !cycles) return fail(LMCE_ERR_INVALID_ARGUMENT, "null pointer");
+  if (reinterpret_cast<uintptr_t>(tensor) % 16 != 0) return fail(LMCE_ERR_INVALID_ARGUMENT, "tensor not 16-byte aligned");
   if (rows < 128 || rows % 128 != 0 || cols < 128 || cols % 128 != 0)
     return fail(LMCE_ERR_INVALID_ARGUMENT, "rows and cols must be positive multiples of 128");
-  if (box_kind != 0 && box_kind != 1) return fail(LMCE_ERR_INVALID_ARGUMENT, "box_kind must be 0 or 1");
+  if (load_kind < 0 || load_kind > 2) return fail(LMCE_ERR_INVALID_ARGUMENT, "load_kind must be 0, 1 or 2");
+  const int piece = load_kind == 0 ? 16384 : 32768;
+  if (stage_bytes < piece || stage_bytes % piece != 0)
+    return fail(LMCE_ERR_INVALID_ARGUMENT, "stage_bytes must be a positive multiple of %d for load_kind %d", piece,
+                load_kind);
+  if (stages < 2 || stages > PROBE_MAX_STAGES) return fail(LMCE_ERR_INVALID_ARGUMENT, "stages must be 2..8");
+  const long long smem = static_cast<long long>(stages) * stage_bytes + 2048;
+  if (smem > PROBE_MAX_SMEM) return fail(LMCE_ERR_INVALID_ARGUMENT, "stages x stage_bytes exceeds shared memory");
+  if (hold_cycles < 0 || hold_cycles > 1000000) return fail(LMCE_ERR_INVALID_ARGUMENT, "hold_cycles out of range");
   if (iters < 16) return fail(LMCE_ERR_INVALID_ARGUMENT, "iters must be at least 16");
   DevInfo* d = nullptr;
   if (int rc = device_info(&d)) return rc;
@@ -1268,14 +1288,20 @@ int lmce_probe_tma_rate(const void* tensor, int64_t rows, int64_t cols, int box_
   CUtensorMap m2, m3;
   if (int rc = make_map(&m2, tensor, false, cols, rows, cols, 128)) return rc;
   if (int rc = make_map_3d(&m3, tensor, false, cols, rows, cols, 128, 2)) return rc;
-  auto kern = tma_rate_probe_kernel;
-  const int smem = PROBE_STAGES * PROBE_STAGE_BYTES + 2048;
+  auto kern = tma_pipeline_probe_kernel;
   static bool done[kMaxDevices] = {};
-  if (int rc = ensure_smem_attr(kern, smem, done)) return rc;
-  kern<<<d->sms, 64, smem, static_cast<cudaStream_t>(stream)>>>(m2, m3, box_kind, iters, static_cast<int>(rows / 128),
-                                                              static_cast<int>(cols / 64), wait_timeout_ns(), cycles,
-                                                              d->err_ptr);
+  if (int rc = ensure_smem_attr(kern, PROBE_MAX_SMEM, done)) return rc;
+  const long long n_pieces32 = rows * cols * 2 / 32768;
+  kern<<<d->sms, 64, static_cast<size_t>(smem), static_cast<cudaStream_t>(stream)>>>(
+      m2, m3, static_cast<const uint8_t*>(tensor), n_pieces32, load_kind, stage_bytes, stages, hold_cycles, iters,
+      static_cast<int>(rows / 128), static_cast<int>(cols / 64), wait_timeout_ns(), cycles, d->err_ptr);
   return launched();
+}
+
+int lmce_probe_tma_rate(const void* tensor, int64_t rows, int64_t cols, int box_kind, int iters,
+                        unsigned long long* cycles, int64_t n_cycles, void* stream) {
+  if (box_kind != 0 && box_kind != 1) return fail(LMCE_ERR_INVALID_ARGUMENT, "box_kind must be 0 or 1");
+  return lmce_probe_tma_pipeline(tensor, rows, cols, box_kind, 32768, 3, 0, iters, cycles, n_cycles, stream);
 }
 
 int lmce_profile_read(void* counters, size_t counter_bytes, void* timeline, size_t timeline_bytes, int reset) {

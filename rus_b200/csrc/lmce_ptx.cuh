@@ -143,6 +143,15 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
+// Plain (untiled) bulk copy of `bytes` contiguous bytes global -> this CTA's shared memory,
+// completion counted on `bar`; both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(smem_dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
 // 2-D tiled bulk-tensor store shared -> global (this GPU's memory), tracked by the
 // thread's bulk async-group. x (innermost, elements) times the element size must be a
 // multiple of 16 bytes; both coordinates must be non-negative.

@@ -7,8 +7,9 @@ whose kernels keep per-CTA cycle counters and a per-tile timeline; csrc/lmce_pro
 runs K forward + backward steps of a bench.py workload through it, and prints where each
 role of the last backward's CTAs spent its cycles: the producer's waits for free stages and
 dependencies, the UMMA issuer's waits for loaded stages and free accumulators, the
-epilogue's work per tile kind, and the per-kind tile durations of the timeline. The counters
-perturb the kernel slightly; use the normal build for timings.
+epilogue's work per tile kind, and the per-kind tile durations of the timeline; then the TMA
+load rate and the stage-ring probe (``lmce_probe_tma_pipeline``). The counters perturb the
+kernel slightly; use the normal build for timings.
 """
 from __future__ import annotations
 
@@ -99,6 +100,33 @@ def tma_rates(dev) -> dict:
     return out
 
 
+# (load kind, stage bytes, stages, hold cycles): the kernels' ring (three 64 KB stages of 3-D
+# boxes, held 1024 cycles as a 256 x 256 pair UMMA with K = 128 holds them) and its neighbours
+PIPELINES = ((1, 65536, 3, 0), (1, 65536, 3, 1024), (0, 65536, 3, 1024), (2, 65536, 3, 0), (2, 65536, 3, 1024),
+             (1, 32768, 6, 512), (0, 32768, 6, 512), (2, 32768, 6, 512), (0, 49152, 4, 1024))
+KIND_NAMES = {0: "2-D {64,128} boxes", 1: "3-D {64,128,2} boxes", 2: "bulk 32 KB copies"}
+
+
+def pipeline_table(dev) -> list:
+    """lmce_probe_tma_pipeline over PIPELINES, from an L2-resident 48 MB tensor and from a
+    768 MB one (DRAM): (source, kind, stage KB, stages, hold, bytes/clk/SM, holder busy %)."""
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    cyc = torch.zeros(sms, dtype=torch.int64, device=dev)
+    iters = 3000
+    rows_out = []
+    for src, rows in (("L2", 16384), ("DRAM", 262144)):
+        t = torch.zeros(rows, 1536, dtype=torch.float16, device=dev)
+        for kind, sb, st, hold in PIPELINES:
+            _lib.call("lmce_probe_tma_pipeline", t.data_ptr(), rows, 1536, kind, sb, st, hold, iters, cyc.data_ptr(),
+                      sms, torch.cuda.current_stream(dev).cuda_stream)
+            torch.cuda.synchronize()
+            c = cyc.double().mean().item()
+            rows_out.append((src, KIND_NAMES[kind], sb // 1024, st, hold, (iters - 9) * sb / c,
+                             100.0 * (iters - 9) * hold / c))
+        del t
+    return rows_out
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--config", default="c2")
@@ -148,6 +176,9 @@ def main(argv=None):
     report(ctr, tl, ms[-1])
     for name, rate in tma_rates(dev).items():
         print(f"TMA load rate, {name} boxes: {rate:.1f} bytes/clk/SM (a 256 x 256 pair UMMA consumes 64)")
+    print("TMA pipeline (ring of stages, each held `hold` cycles after it lands):")
+    for src, kind, kb, st, hold, rate, busy in pipeline_table(dev):
+        print(f"  {src:4s} {kind:22s} {st} x {kb:2d} KB hold {hold:4d}: {rate:5.1f} bytes/clk/SM, holder busy {busy:5.1f}%")
 
 
 if __name__ == "__main__":

@@ -46,6 +46,12 @@ def test_argument_validation_without_gpu():
     assert rc == _lib.LMCE_ERR_UNSUPPORTED  # hidden_dim not a multiple of 64
     rc = lib.lmce_backward(16, 16, 16, 16, 10, 128, 100, 0, 0, None, 16, None, None, None, 8192, 16, 16, None)
     assert rc == _lib.LMCE_ERR_WORKSPACE
+    # the stage-ring probe rejects rings that do not fit shared memory and stages that are not
+    # whole pieces of the load kind, before touching a device
+    cyc = (ctypes.c_ulonglong * 256)()
+    for kind, stage, stages in ((1, 65536, 4), (1, 49152, 4), (0, 8192, 3), (3, 32768, 3), (2, 32768, 9)):
+        rc = lib.lmce_probe_tma_pipeline(256, 1024, 1536, kind, stage, stages, 0, 100, cyc, 256, None)
+        assert rc == _lib.LMCE_ERR_INVALID_ARGUMENT, (kind, stage, stages)
 
 
 def test_default_workspace_holds_no_logits_sized_buffer():
