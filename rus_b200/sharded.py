@@ -10,8 +10,8 @@ hidden states and labels are replicated. The two exchange steps:
 * backward: each rank contracts its shard's gradient tile into its local dW
   shard and an fp32 dX contribution, which is summed over the ranks. On GPUs
   that share an NVLink switch with multicast (NVLS) support, for dX of at least
-  32 MiB in fp32 (``LMCE_NVLS=1`` forces it, ``0`` disables it), the sum is
-  fused into the backward kernel (``lmce_backward_nvls``):
+  32 MiB in fp32 or groups of at least 8 GPUs (``LMCE_NVLS=1`` forces it, ``0``
+  disables it), the sum is fused into the backward kernel (``lmce_backward_nvls``):
   as a row block's last-chunk dX tiles finish on every rank, each rank sums its
   slice of the block's columns over the GPUs through the switch
   (``multimem.ld_reduce``) and stores the result to every GPU's output copy
@@ -20,9 +20,10 @@ hidden states and labels are replicated. The two exchange steps:
   when a call has more tokens than they hold. Otherwise one
   NCCL all-reduce sums the fp32 contributions after the kernel and
   ``lmce_dx_finalize`` casts them to the input dtype. Measured at the config-2 shape
-  (ms per step, fused / NCCL): 8 GPUs, 16384 tokens (dX 100 MB) 3.58 / 3.90; 4 GPUs,
-  8192 tokens (50 MB) 3.24 / 3.58; 2 GPUs, 4096 tokens (25 MB) 3.11 / 3.04; 2048
-  tokens (12.6 MB) on 4 and 8 GPUs 0.97 / 0.89 and 0.84 / 0.80; hence the size rule.
+  (backward phase, fused / NCCL, ms per step, one box of B200s): 2048 tokens (dX 12.6 MB)
+  on 2, 4 and 8 GPUs 1.098 / 1.086, 0.630 / 0.606 and 0.383 / 0.510; earlier kernels gave,
+  per step, 16384 tokens (100 MB) on 8 GPUs 3.58 / 3.90 and 8192 tokens (50 MB) on 4 GPUs
+  3.24 / 3.58; hence the rule.
 
 The reference has no multi-GPU path (it pins one T4); this is the B200 build's
 addition for the same operator interface.
@@ -111,19 +112,21 @@ def exchange_capacity(n: int, current: int = 0) -> int:
 
 
 NVLS_MIN_DX_BYTES = 32 << 20  # fp32 dX size from which the fused exchange beats NCCL's all-reduce
+NVLS_MIN_WORLD = 8  # group size from which it wins at any size
 
 
 def nvls_dx_exchange(n: int, h: int, dtype: torch.dtype, device: torch.device, group=None):
     """The group's ``NvlsDxExchange`` for n tokens, or None when the fused exchange is not
-    used: LMCE_NVLS=0, or (default) fp32 dX below NVLS_MIN_DX_BYTES, or the group cannot use
-    NVLink SHARP (decided jointly, so every rank takes the same path). LMCE_NVLS=1 uses it
+    used: LMCE_NVLS=0, or (default) fp32 dX below NVLS_MIN_DX_BYTES in a group of fewer than
+    NVLS_MIN_WORLD ranks, or the group cannot use NVLink SHARP (decided jointly, so every rank
+    takes the same path). LMCE_NVLS=1 uses it
     whenever the GPUs support it. One buffer per (device, group, h, dtype), reused for any n
     up to its capacity and replaced by one 1.5x larger when n outgrows it (every rank sees
     the same n, so all ranks reallocate together)."""
     mode = os.environ.get("LMCE_NVLS", "auto")
     if mode == "0" or device.type != "cuda":
         return None
-    if mode != "1" and 4 * n * h < NVLS_MIN_DX_BYTES:
+    if mode != "1" and 4 * n * h < NVLS_MIN_DX_BYTES and dist.get_world_size(group) < NVLS_MIN_WORLD:
         return None
     key = (device.index, _group_name(group), h, dtype)
     cached = _NVLS_CACHE.get(key, False)
