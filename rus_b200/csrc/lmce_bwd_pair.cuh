@@ -25,8 +25,11 @@
 //   DW(c)   vocab block jv (M) x hidden block p (N = 256) of dW = G_c^T . X_lab, K =
 //           labelled tokens (new: the reference returns None for the weight, ops.py:339)
 // The tile list, its order, the dependency counters and the fused cross-GPU exchange
-// follow lmce_bwd_kernel; every count covers both CTAs of a pair (each CTA publishes
-// its half). The pair leader (cluster rank 0) claims tickets, checks dependencies and
+// follow lmce_bwd_kernel; every count covers both CTAs of a pair: each epilogue warp
+// publishes its rows of a GT tile (no CTA barrier: 16 counts per tile), each CTA its half of
+// a DXT tile, and a tile that read a G buffer releases it when its accumulator is full (the
+// UMMAs have read their operands by then). The pair leader (cluster rank 0) claims
+// tickets, checks dependencies and
 // hands each tile to both CTAs' schedule rings (the peer's through distributed shared
 // memory); only the leader issues UMMAs. Every wait is bounded.
 #pragma once
@@ -44,6 +47,7 @@ constexpr int P_KB = 2 * BK;     // K per stage
 constexpr int P_STAGES = 3;
 constexpr int P_THREADS = 320;  // warp 0 producer, warp 1 UMMA, warps 2-9 epilogue (two per TMEM lane quadrant)
 constexpr int P_EPI = 256;
+constexpr int P_EPI_WARPS = P_EPI / 32;
 constexpr int P_A_BYTES = BM * P_KB * 2;                   // 128 rows x 128 k: 32 KB
 constexpr int P_B_BYTES = BM * P_KB * 2;                   // up to 128 rows (N / 2) x 128 k: 32 KB
 constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;       // 64 KB
@@ -253,7 +257,7 @@ template <bool BF16>
 __global__ void __launch_bounds__(P_THREADS, 1)
     lmce_bwd_pair_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
                          const __grid_constant__ CUtensorMap map_g, const __grid_constant__ CUtensorMap map_dx,
-                         const BwdParams p) {
+                         const __grid_constant__ CUtensorMap map_dw, const BwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + P_STAGES * P_STAGE_BYTES);
@@ -305,6 +309,7 @@ __global__ void __launch_bounds__(P_THREADS, 1)
     tma_prefetch_desc(&map_x);
     tma_prefetch_desc(&map_g);
     tma_prefetch_desc(&map_dx);
+    if (p.want_dw) tma_prefetch_desc(&map_dw);
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_holder, TMEM_COLS);
@@ -355,7 +360,7 @@ __global__ void __launch_bounds__(P_THREADS, 1)
             }
             LMCE_PROF(pc_dep_g += clock64() - pt0;)
           } else if ((t.kind == BK_DX || t.kind == BK_DW) && t.chunk > g_ready_chunk) {
-            ok = wait_counter(&gdone[t.chunk], 2 * geo.nG(t.chunk), abort_flag, tlimit);
+            ok = wait_counter(&gdone[t.chunk], 2 * P_EPI_WARPS * geo.nG(t.chunk), abort_flag, tlimit);
             if (ok) g_ready_chunk = t.chunk;
             acquired = true;
             LMCE_PROF(pc_dep_gd += clock64() - pt0;)
@@ -537,6 +542,7 @@ __global__ void __launch_bounds__(P_THREADS, 1)
     int slot = 0, acc = 0;
     uint32_t sphase = 0, acc_phase = 0;
     bool ok = true;
+    bool dw_pending = false;  // this warp's last dW tile may still have TMA stores reading its slice
     LMCE_PROF(long long e_sched = 0, e_chain = 0, e_xch = 0, tf_g = 0, tf_dx = 0, tf_dw = 0, wk_g = 0, wk_dx = 0,
               wk_dw = 0, n_g = 0, n_dx = 0, n_dw = 0;
               int tl_i = 0; const long long pl0 = clock64(); long long pe_tile = 0; unsigned long long* tle = nullptr;)
@@ -554,6 +560,11 @@ __global__ void __launch_bounds__(P_THREADS, 1)
         sphase ^= 1u;
       }
       if (t.kind == BK_END) break;
+      if (dw_pending) {  // the last dW tile's TMA stores have left this warp's slice
+        if (lane == 0) bulk_wait_read_all();
+        __syncwarp();
+        dw_pending = false;
+      }
       LMCE_PROF(tle = et == 0 ? prof_entry(tl_i++) : nullptr;
                 if (tle) { tle[0] = t.kind; tle[1] = t.chunk; tle[2] = t.m; tle[3] = t.n; tle[5] = global_timer_ns(); })
       if (t.kind == BK_XCH) {
@@ -630,6 +641,10 @@ __global__ void __launch_bounds__(P_THREADS, 1)
                 if (tle) tle[6] = global_timer_ns();)
       tc_fence_after();
       const uint32_t taddr = tmem_base + lane_base + static_cast<uint32_t>(acc * BN);
+      // A DXT or dW tile releases its G buffer as soon as its accumulator is full: its UMMAs have
+      // read all of their G operand by then (TMA loads that completed before they were issued),
+      // so the release waits for none of the tile's stores.
+      if ((t.kind == BK_DW || t.kind == BK_DX) && et == 0) atomicAdd(&consumed[t.chunk], 1);
 
 #pragma unroll 1
       for (int c = c_lo; c < c_hi; ++c) {
@@ -732,15 +747,30 @@ __global__ void __launch_bounds__(P_THREADS, 1)
             }
           }
         } else {  // BK_DW: this thread: vocab row of the chunk; columns: hidden h0 + j
+          // The warp's 32 rows x 32 columns leave by one TMA store of a 64-byte-swizzled box
+          // (16-byte piece i of row r at position i ^ ((r / 2) % 4): conflict-free), through
+          // two 2 KB halves of its slice used in turn; rows past the shard are clipped by TMA.
           const int h0 = t.n * BN + c * 32;
-          if (h0 < p.H) {
+          const int v0 = t.m * P_RB + BM * static_cast<int>(rank) + q * 32;  // warp's first vocab row
+          if (h0 < p.H && v0 < w) {
+            uint8_t* half = xstage + ((c - c_lo) & 1) * 2048;
+            if (c - c_lo >= 2 && lane == 0) bulk_wait_read_1();  // the box of two chunks ago has left it
+            __syncwarp();
+            uint4* row = reinterpret_cast<uint4*>(half + lane * 64);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] *= dscale;
-            const int v0 = t.m * P_RB + BM * static_cast<int>(rank) + q * 32;  // warp's first vocab row
-            char* dbase = reinterpret_cast<char*>(p.dw_out) +
-                          ((static_cast<size_t>(t.chunk) * p.v_chunk + v0) * p.H + h0) * 2;
-            store_rows32<BF16>(xstage, v, dbase, static_cast<size_t>(p.H) * 2, 0, lane,
-                               [v0, w](int rr) { return v0 + rr < w; });
+            for (int i = 0; i < 4; ++i)
+              row[i ^ ((lane >> 1) & 3)] =
+                  make_uint4(pack2<BF16>(v[8 * i] * dscale, v[8 * i + 1] * dscale),
+                             pack2<BF16>(v[8 * i + 2] * dscale, v[8 * i + 3] * dscale),
+                             pack2<BF16>(v[8 * i + 4] * dscale, v[8 * i + 5] * dscale),
+                             pack2<BF16>(v[8 * i + 6] * dscale, v[8 * i + 7] * dscale));
+            fence_async_shared();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&map_dw, half, h0, t.chunk * p.v_chunk + v0);
+              bulk_commit_group();
+            }
+            dw_pending = true;
           }
         }
       }
@@ -750,18 +780,20 @@ __global__ void __launch_bounds__(P_THREADS, 1)
         acc = 0;
         acc_phase ^= 1u;
       }
-      // publish this CTA's half of the tile
-      if (t.kind == BK_DX && !dx_last && lane == 0) {
-        bulk_wait_all();       // this warp's TMA stores / adds of the tile are done in global memory
-        fence_async_global();  // and ordered before the publishing thread's fence and count
-      }
-      named_bar<1, P_EPI>();  // all of this CTA's stores of the tile happen before its count
+      // publish: a GT tile per warp (each warp's G^T rows, counted 8 times per CTA), a DXT tile
+      // per CTA (after all eight warps' TMA stores / adds); dW tiles have nothing to publish
       if (t.kind == BK_G) {
-        if (et == 0) {
+        __syncwarp();
+        if (lane == 0) {
           __threadfence();
           atomicAdd(&gdone[t.chunk], 1);
         }
       } else if (t.kind == BK_DX) {
+        if (!dx_last && lane == 0) {
+          bulk_wait_all();       // this warp's TMA stores / adds of the tile are done in global memory
+          fence_async_global();  // and ordered before the publishing thread's fence and count
+        }
+        named_bar<1, P_EPI>();  // all of this CTA's stores of the tile happen before its count
         if (et == 0) {
           const bool x_last = geo.xch && t.chunk + 1 == geo.C;
           if (x_last)
@@ -769,15 +801,11 @@ __global__ void __launch_bounds__(P_THREADS, 1)
           else
             __threadfence();
           atomicAdd(&dxchain[t.m * geo.nh + t.n], 1);
-          atomicAdd(&consumed[t.chunk], 1);
           if (x_last)
             multimem_st_release_b32(p.x_flags_mc + p.x_world +
                                         ((static_cast<size_t>(t.m) * p.x_world + p.x_rank) * geo.nh + t.n) * 2 + rank,
                                     p.x_epoch);
         }
-      } else if (et == 0) {
-        __threadfence();
-        atomicAdd(&consumed[t.chunk], 1);
       }
       LMCE_PROF(const long long dwk = clock64() - pe_tile;
                 if (t.kind == BK_G) { wk_g += dwk; ++n_g; } else if (t.kind == BK_DX) { wk_dx += dwk; ++n_dx; }

@@ -185,6 +185,22 @@ int make_map_f32(CUtensorMap* m, void* base, uint64_t inner, uint64_t outer, uin
   return LMCE_OK;
 }
 
+// A [outer][inner] tensor of 16-bit elements as the target of 32 x 32 TMA stores from a
+// 64-byte-swizzled shared-memory box (the CTA-pair backward's dW epilogue).
+int make_map_store16(CUtensorMap* m, void* base, bool bf16, uint64_t inner, uint64_t outer, uint64_t ld_elems) {
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0) return fail(LMCE_ERR_INVALID_ARGUMENT, "tensor base not 16B aligned");
+  if ((ld_elems * 2) % 16 != 0) return fail(LMCE_ERR_INVALID_ARGUMENT, "row stride not a multiple of 16 bytes");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld_elems * 2};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(LMCE_ERR_CUDA, "cuTensorMapEncodeTiled (store) failed (%d)", static_cast<int>(r));
+  return LMCE_OK;
+}
+
 // The same [outer][inner] tensor of 16-bit elements as a 3-D view {64 elements, outer,
 // inner / 64 blocks at a 128-byte stride}, box {64, box_y, box_z}, 128-byte swizzle: a box
 // reads box_z * 128 contiguous bytes of each of its box_y rows.
@@ -325,7 +341,7 @@ int launch_bwd_pair(const CUtensorMap* maps, const BwdParams& p, int sms, cudaSt
   if (int rc = ensure_smem_attr(kern, smem, done)) return rc;
   const int pairs = max_pairs(kern, smem, sms, pairs_cache, P_THREADS);
   timing_mark(1, 0, st);
-  const int rc = launch_ex(kern, 2 * pairs, P_THREADS, smem, 2, st, maps[0], maps[1], maps[2], maps[3], p);
+  const int rc = launch_ex(kern, 2 * pairs, P_THREADS, smem, 2, st, maps[0], maps[1], maps[2], maps[3], maps[4], p);
   timing_mark(1, 1, st);
   return rc;
 }
@@ -951,6 +967,7 @@ int backward_impl(const void* hidden, const void* weight, const int64_t* labels,
   // (buffer b starts at vocab row b * v_chunk), for the one-CTA kernel G
   // [NUM_GBUF * rows_pad, v_chunk] (buffer b starts at token row b * rows_pad).
   CUtensorMap maps[7];
+  std::memset(maps, 0, sizeof(maps));
   const int g_rows = NUM_GBUF * L.rows_pad;
   const int gt_rows = NUM_GBUF * L.v_chunk;
   const bool pair = use_pair_backward(h);
@@ -964,6 +981,9 @@ int backward_impl(const void* hidden, const void* weight, const int64_t* labels,
     if (int rc = make_map_3d(&maps[2], g, bf16, L.rows_pad, gt_rows, L.rows_pad, 128, 2)) return rc;
     // the fp32 dX^T accumulator [H][rows_pad], 32 x 32 boxes for the epilogue's TMA stores and adds
     if (int rc = make_map_f32(&maps[3], dx_acc, L.rows_pad, h, L.rows_pad, 32, 32)) return rc;
+    // dW [V][H]: 32 x 32 boxes for the epilogue's TMA stores
+    if (d_weight != nullptr)
+      if (int rc = make_map_store16(&maps[4], d_weight, bf16, h, vl, h)) return rc;
   } else {
     // x K-major, x MN-major, W K-major, W MN-major, G K-major, G MN-major (X and W fall
     // back to 2-D MN-major maps when H is below 256)

@@ -173,6 +173,9 @@ __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const 
 
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 
+// Wait until at most one of this thread's committed bulk groups still reads shared memory.
+__device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+
 // Wait until this thread's committed bulk stores / reductions have finished reading shared memory.
 __device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 
