@@ -149,77 +149,130 @@ def make_config(cfg: str, device, replicas: int = 1, seed: int = 0):
 
 # ------------------------------------------------------------------ clocks
 
+# NVML sampling loop run in a child process (no GIL shared with the ranks' host work): argv[1]
+# lists the GPUs as domain:bus:device, argv[2] the period in seconds. It prints one JSON line
+# when ready, starts sampling when a line arrives on its stdin and, once its stdin closes,
+# prints one JSON line of samples per GPU.
+_SAMPLER_SRC = r"""
+import json, select, sys
+import pynvml
+pynvml.nvmlInit()
+want = [tuple(int(v) for v in w.split(":")) for w in sys.argv[1].split(",")]
+period = float(sys.argv[2])
+found = {}
+for i in range(pynvml.nvmlDeviceGetCount()):
+    h = pynvml.nvmlDeviceGetHandleByIndex(i)
+    pci = pynvml.nvmlDeviceGetPciInfo(h)
+    found[(int(pci.domain), int(pci.bus), int(pci.device))] = h
+handles = [found[w] for w in want]
+mx = [float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)) for h in handles]
+print(json.dumps({"max_mhz": mx}), flush=True)
+sys.stdin.readline()
+samples = [[] for _ in handles]
+while not select.select([sys.stdin], [], [], period)[0]:
+    for k, h in enumerate(handles):
+        try:
+            samples[k].append((float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)),
+                               int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(h))))
+        except Exception:
+            pass
+print(json.dumps({"samples": samples}), flush=True)
+"""
+
+
+def pci_ids(devices) -> list:
+    """domain:bus:device of each CUDA device (how the sampler finds its NVML handle)."""
+    out = []
+    for dev in devices:
+        props = torch.cuda.get_device_properties(dev)
+        out.append(f"{int(props.pci_domain_id)}:{int(props.pci_bus_id)}:{int(props.pci_device_id)}")
+    return out
+
+
 class ClockSampler:
-    """SM clock and clock-event reasons sampled (NVML) every ~2 ms while the timed region runs."""
+    """SM clock and clock-event reasons of one or more GPUs, sampled (NVML) every ~2 ms by a
+    child process between start() and stop(). The child is set up (NVML initialised, handles
+    found: tens to hundreds of ms) when the sampler is entered, which must come before the
+    ranks' last barrier ahead of the timed region: a rank that did that set-up inside the
+    timed region would start its steps late, and under torchrun the other ranks would wait
+    for it at the first collective, inflating their step times. Under torchrun rank 0 samples
+    every rank's GPU and the other ranks sample none."""
 
     REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown"}
 
-    def __init__(self, device: torch.device, period_s: float = 0.002):
-        self.device = device
+    def __init__(self, devices, period_s: float = 0.002):
+        self.devices = list(devices)
         self.period = period_s
-        self.samples = []
-        self.max_mhz = None
-        self._stop = None
-        self._thread = None
+        self.samples = [[] for _ in self.devices]
+        self.max_mhz = [None for _ in self.devices]
+        self._proc = None
 
     def __enter__(self):
-        import threading
+        import subprocess
 
-        try:
-            import pynvml
-
-            pynvml.nvmlInit()
-            # match the CUDA device to its NVML handle by PCI domain / bus / device numbers
-            props = torch.cuda.get_device_properties(self.device)
-            want = (int(getattr(props, "pci_domain_id", -1)), int(getattr(props, "pci_bus_id", -1)),
-                    int(getattr(props, "pci_device_id", -1)))
-            h = None
-            for i in range(pynvml.nvmlDeviceGetCount()):
-                cand = pynvml.nvmlDeviceGetHandleByIndex(i)
-                pci = pynvml.nvmlDeviceGetPciInfo(cand)
-                if (int(pci.domain), int(pci.bus), int(pci.device)) == want:
-                    h = cand
-                    break
-            if h is None:
-                h = pynvml.nvmlDeviceGetHandleByIndex(self.device.index or 0)
-            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
-        except Exception:
+        if not self.devices:
             return self
-        self._stop = threading.Event()
-
-        def run():
-            while not self._stop.is_set():
-                try:
-                    mhz = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
-                    reasons = int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(h))
-                    self.samples.append((mhz, reasons))
-                except Exception:
-                    pass
-                self._stop.wait(self.period)
-
-        self._thread = threading.Thread(target=run, daemon=True)
-        self._thread.start()
+        try:
+            pci = pci_ids(self.devices)
+            self._proc = subprocess.Popen([sys.executable, "-c", _SAMPLER_SRC, ",".join(pci), str(self.period)],
+                                          stdin=subprocess.PIPE, stdout=subprocess.PIPE,
+                                          stderr=subprocess.DEVNULL, text=True)
+            ready = json.loads(self._proc.stdout.readline())
+            self.max_mhz = ready["max_mhz"]
+        except Exception:
+            self._stop_proc()
         return self
 
+    def start(self):
+        """Begin sampling (call at the start of the timed region)."""
+        if self._proc is not None:
+            try:
+                self._proc.stdin.write("go\n")
+                self._proc.stdin.flush()
+            except Exception:
+                self._stop_proc()
+
+    def _stop_proc(self):
+        if self._proc is None:
+            return None
+        out = None
+        try:
+            out, _ = self._proc.communicate(input="", timeout=10)
+        except Exception:
+            self._proc.kill()
+            self._proc.wait()
+        self._proc = None
+        return out
+
+    def stop(self):
+        """End sampling and collect the samples (call at the end of the timed region)."""
+        out = self._stop_proc()
+        if out:
+            try:
+                got = json.loads(out.strip().splitlines()[-1])["samples"]
+                self.samples = [[(float(m), int(r)) for m, r in g] for g in got]
+            except Exception:
+                pass
+
     def __exit__(self, *exc):
-        if self._thread is not None:
-            self._stop.set()
-            self._thread.join(timeout=2)
+        self.stop()
         return False
 
-    def summary(self):
-        if not self.samples:
-            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"], "samples": 0}
+    def summary(self, k: int = 0):
+        samples = self.samples[k] if k < len(self.samples) else []
+        mx = self.max_mhz[k] if k < len(self.max_mhz) else None
+        if not samples:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": ["unavailable"], "samples": 0}
         reasons = set()
         capped = 0
-        for _, r in self.samples:
+        for _, r in samples:
             for bit, name in self.REASONS.items():
                 if r & bit:
                     reasons.add(name)
             capped += 1 if r & 0x4 else 0
-        return {"sm_mhz": statistics.median(m for m, _ in self.samples), "sm_max_mhz": self.max_mhz,
-                "reasons": sorted(reasons), "samples": len(self.samples),
-                "power_capped_fraction": capped / len(self.samples), "source": "nvml, ~2 ms"}
+        return {"sm_mhz": statistics.median(m for m, _ in samples), "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(samples),
+                "power_capped_fraction": capped / len(samples), "source": "nvml, ~2 ms, child process"}
 
 
 def choose_peak(peaks: dict, clk: dict):
@@ -466,9 +519,14 @@ def main():
             _lib.call("lmce_set_timing_events", k, None, None)
 
     half = args.steps // 2
-    torch.cuda.synchronize()
-    barrier()
-    with ClockSampler(device) as clk:
+    # one sampling process per job: rank 0 samples every rank's GPU (one process per GPU of one
+    # node, rank r on cuda:r), the other ranks none; it is set up before the last barrier, so
+    # every rank enters the timed region together
+    sampled = [device] if world == 1 else ([torch.device("cuda", r) for r in range(world)] if rank == 0 else [])
+    with ClockSampler(sampled) as clk:
+        torch.cuda.synchronize()
+        barrier()
+        clk.start()
         value_steps(0, half)
         barrier()
         launches = _lib.launch_count() - l0
@@ -482,6 +540,7 @@ def main():
         stage("timed steps (second half)")
         value_steps(half, args.steps)
         barrier()
+        clk.stop()
         launches += _lib.launch_count() - l1
     step_ms = [a.elapsed_time(b) for a, b in ev]
     kern_ms = {k: statistics.mean(a.elapsed_time(b) for a, b in kev[k]) for k in (0, 1)}
@@ -508,6 +567,9 @@ def main():
     # ---- roofline of the dominant kernel (largest share of the step)
     peaks, peak_src = load_peaks()
     clocks = clk.summary()
+    if world > 1 and rank == 0:
+        clocks["per_gpu"] = [{k: clk.summary(r).get(k) for k in ("sm_mhz", "reasons", "power_capped_fraction")}
+                             for r in range(world)]
     k_peak, peak_kind = choose_peak(peaks, clocks)
     burst = float(peaks["bf16_tflops"])
     sust = float(peaks.get("bf16_tflops_sustained", burst))
@@ -541,14 +603,16 @@ def main():
     per_rank = None
     if world > 1:
         mine = torch.tensor([statistics.mean(step_ms), kern_ms[0], kern_ms[1], fwd_phase_ms, bwd_phase_ms,
-                             float(clocks.get("sm_mhz") or 0.0), 1e3 * host_s[0] / args.steps,
-                             1e3 * host_s[1] / args.steps], dtype=torch.float64, device=device)
+                             1e3 * host_s[0] / args.steps, 1e3 * host_s[1] / args.steps],
+                            dtype=torch.float64, device=device)
         allr = torch.empty((world, mine.numel()), dtype=torch.float64, device=device)
         dist.all_gather_into_tensor(allr, mine)
         cols = allr.t().tolist()
         per_rank = {k: [round(v, 4) for v in c] for k, c in
                     zip(("step_ms", "stats_ms", "backward_ms", "forward_phase_ms", "backward_phase_ms",
-                         "sm_mhz", "host_forward_ms", "host_backward_ms"), cols)}
+                         "host_forward_ms", "host_backward_ms"), cols)}
+        if rank == 0:
+            per_rank["sm_mhz"] = [clk.summary(r).get("sm_mhz") for r in range(world)]
         dist.barrier(device_ids=[local_rank])
     err = _lib.device_error(reset=True)
     if err:

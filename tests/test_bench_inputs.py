@@ -46,3 +46,35 @@ def test_peak_choice_follows_the_clock_record():
     capped = bench.choose_peak(peaks, {"sm_mhz": 1350.0, "sm_max_mhz": 1965.0, "power_capped_fraction": 0.9})
     assert burst[0] == 1635.7 and "burst" in burst[1]
     assert capped[0] == 1396.7 and "sustained" in capped[1]
+
+
+def test_clock_sampler_child_process(tmp_path, monkeypatch):
+    """The clock sampler runs NVML in a child process (no interpreter lock shared with the
+    thread that issues the GPU work) and returns per-GPU samples with their clock-event
+    reasons; checked here against a stand-in NVML module on the host."""
+    (tmp_path / "pynvml.py").write_text(
+        "NVML_CLOCK_SM = 1\n"
+        "class _P:\n"
+        "    def __init__(self, i): self.domain, self.bus, self.device = 0, 10 + i, 0\n"
+        "def nvmlInit(): pass\n"
+        "def nvmlDeviceGetCount(): return 2\n"
+        "def nvmlDeviceGetHandleByIndex(i): return i\n"
+        "def nvmlDeviceGetPciInfo(h): return _P(h)\n"
+        "def nvmlDeviceGetMaxClockInfo(h, c): return 1965\n"
+        "def nvmlDeviceGetClockInfo(h, c): return 1800 + 100 * h\n"
+        "def nvmlDeviceGetCurrentClocksEventReasons(h): return 4 * h\n")
+    monkeypatch.setenv("PYTHONPATH", str(tmp_path))
+    monkeypatch.setattr(bench, "pci_ids", lambda devs: ["0:11:0", "0:10:0"][:len(devs)])
+    import time
+
+    with bench.ClockSampler([0, 1]) as clk:
+        time.sleep(0.05)
+        assert clk.summary(0)["samples"] == 0  # set up, not sampling before start()
+        clk.start()
+        time.sleep(0.05)
+        clk.stop()
+    a, b = clk.summary(0), clk.summary(1)
+    assert a["samples"] > 3 and b["samples"] > 3
+    assert a["sm_mhz"] == 1900.0 and a["reasons"] == ["sw_power_cap"] and a["power_capped_fraction"] == 1.0
+    assert b["sm_mhz"] == 1800.0 and b["reasons"] == [] and b["sm_max_mhz"] == 1965.0
+    assert bench.ClockSampler([]).summary()["samples"] == 0
