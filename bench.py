@@ -72,8 +72,8 @@ PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # DRAM bytes (read + write) of one forward-statistics launch and of one backward launch at
 # config 2 with the default chunk, from one `ncu --set full` capture
 # (dram__bytes_read.sum + dram__bytes_write.sum) of this script's second warm-up step.
-FWD_STATS_TRAFFIC_C2 = 503_315_456 + 5_543_168
-BWD_TRAFFIC_C2 = 1_828_120_576 + 1_257_360_896
+FWD_STATS_TRAFFIC_C2 = 504_412_000 + 5_608_000
+BWD_TRAFFIC_C2 = 1_822_938_000 + 1_257_441_000
 CPU_BUDGET_S = 150.0  # CPU seconds the reference arm may spend (warm-up + timed steps)
 
 

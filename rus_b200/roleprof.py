@@ -83,33 +83,48 @@ def report(ctr, tl, bwd_ms):
             print(f"  {name} tiles {len(a)}: UMMA span per tile {a.mean():.2f} us mean, {np.median(a):.2f} median")
 
 
+def _timed(dev, fn):
+    """Run fn() on the current stream; (elapsed ns) from CUDA events around it."""
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) * 1e6
+
+
 def tma_rates(dev) -> dict:
-    """Bytes per clock per SM that TMA delivers from an L2-resident 48 MB tensor, for the two
-    box shapes (lmce_probe_tma_rate): 2-D {64, 128} (128-byte row segments) and the kernels'
-    3-D {64, 128, 2} (256-byte row segments)."""
+    """TMA delivery from an L2-resident 48 MB tensor for the two box shapes
+    (lmce_probe_tma_rate): 2-D {64, 128} (128-byte row segments) and the kernels' 3-D
+    {64, 128, 2} (256-byte row segments): (bytes per SM clock, bytes per ns per SM, SM GHz)."""
     t = torch.zeros(16384, 1536, dtype=torch.float16, device=dev)
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
     cyc = torch.zeros(sms, dtype=torch.int64, device=dev)
     iters = 4000
     out = {}
     for kind, name in ((0, "2-D {64,128} x2"), (1, "3-D {64,128,2}")):
-        _lib.call("lmce_probe_tma_rate", t.data_ptr(), 16384, 1536, kind, iters, cyc.data_ptr(), sms,
-                  torch.cuda.current_stream(dev).cuda_stream)
-        torch.cuda.synchronize()
-        out[name] = (iters - 9) * 32768 / cyc.double().mean().item()
+        ns = _timed(dev, lambda: _lib.call("lmce_probe_tma_rate", t.data_ptr(), 16384, 1536, kind, iters,
+                                           cyc.data_ptr(), sms, torch.cuda.current_stream(dev).cuda_stream))
+        c = cyc.double().mean().item()
+        out[name] = ((iters - 9) * 32768 / c, iters * 32768 / ns, c / ns * iters / (iters - 9))
     return out
 
 
 # (load kind, stage bytes, stages, hold cycles): the kernels' ring (three 64 KB stages of 3-D
-# boxes, held 1024 cycles as a 256 x 256 pair UMMA with K = 128 holds them) and its neighbours
-PIPELINES = ((1, 65536, 3, 0), (1, 65536, 3, 1024), (0, 65536, 3, 1024), (2, 65536, 3, 0), (2, 65536, 3, 1024),
+# boxes, held 1024 cycles as a 256 x 256 pair UMMA with K = 128 holds them; 1536 cycles at the
+# probe's full clock last as long as 1024 at the ~1.3 GHz the kernels run at under the power
+# cap) and its neighbours
+PIPELINES = ((1, 65536, 3, 0), (1, 65536, 3, 1024), (1, 65536, 3, 1536), (0, 65536, 3, 1024), (2, 65536, 3, 0),
+             (2, 65536, 3, 1024),
              (1, 32768, 6, 512), (0, 32768, 6, 512), (2, 32768, 6, 512), (0, 49152, 4, 1024))
 KIND_NAMES = {0: "2-D {64,128} boxes", 1: "3-D {64,128,2} boxes", 2: "bulk 32 KB copies"}
 
 
 def pipeline_table(dev) -> list:
     """lmce_probe_tma_pipeline over PIPELINES, from an L2-resident 48 MB tensor and from a
-    768 MB one (DRAM): (source, kind, stage KB, stages, hold, bytes/clk/SM, holder busy %)."""
+    768 MB one (DRAM): (source, kind, stage KB, stages, hold, bytes/clk/SM, holder busy %,
+    bytes/ns/SM, SM GHz). Bytes per SM clock depend on the SM clock (the memory system keeps
+    its own), so the clock of each run is reported with it."""
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
     cyc = torch.zeros(sms, dtype=torch.int64, device=dev)
     iters = 3000
@@ -117,12 +132,12 @@ def pipeline_table(dev) -> list:
     for src, rows in (("L2", 16384), ("DRAM", 262144)):
         t = torch.zeros(rows, 1536, dtype=torch.float16, device=dev)
         for kind, sb, st, hold in PIPELINES:
-            _lib.call("lmce_probe_tma_pipeline", t.data_ptr(), rows, 1536, kind, sb, st, hold, iters, cyc.data_ptr(),
-                      sms, torch.cuda.current_stream(dev).cuda_stream)
-            torch.cuda.synchronize()
+            ns = _timed(dev, lambda: _lib.call("lmce_probe_tma_pipeline", t.data_ptr(), rows, 1536, kind, sb, st,
+                                               hold, iters, cyc.data_ptr(), sms,
+                                               torch.cuda.current_stream(dev).cuda_stream))
             c = cyc.double().mean().item()
             rows_out.append((src, KIND_NAMES[kind], sb // 1024, st, hold, (iters - 9) * sb / c,
-                             100.0 * (iters - 9) * hold / c))
+                             100.0 * (iters - 9) * hold / c, iters * sb / ns, c / ns * iters / (iters - 9)))
         del t
     return rows_out
 
@@ -174,11 +189,13 @@ def main(argv=None):
     print(f"{args.config}, v_chunk {args.v_chunk or 'default'}: backward median {statistics.median(ms):.3f} ms "
           f"over {args.steps} steps")
     report(ctr, tl, ms[-1])
-    for name, rate in tma_rates(dev).items():
-        print(f"TMA load rate, {name} boxes: {rate:.1f} bytes/clk/SM (a 256 x 256 pair UMMA consumes 64)")
+    for name, (rate, per_ns, ghz) in tma_rates(dev).items():
+        print(f"TMA load rate, {name} boxes: {rate:.1f} bytes/clk/SM = {per_ns:.1f} bytes/ns/SM at {ghz:.2f} GHz "
+              f"(a 256 x 256 pair UMMA consumes 64 bytes/clk/SM)")
     print("TMA pipeline (ring of stages, each held `hold` cycles after it lands):")
-    for src, kind, kb, st, hold, rate, busy in pipeline_table(dev):
-        print(f"  {src:4s} {kind:22s} {st} x {kb:2d} KB hold {hold:4d}: {rate:5.1f} bytes/clk/SM, holder busy {busy:5.1f}%")
+    for src, kind, kb, st, hold, rate, busy, per_ns, ghz in pipeline_table(dev):
+        print(f"  {src:4s} {kind:22s} {st} x {kb:2d} KB hold {hold:4d}: {rate:5.1f} bytes/clk/SM = "
+              f"{per_ns:5.1f} bytes/ns/SM at {ghz:.2f} GHz, holder busy {busy:5.1f}%")
 
 
 if __name__ == "__main__":
