@@ -26,12 +26,12 @@
 //           labelled tokens (new: the reference returns None for the weight, ops.py:339)
 // The tile list, its order, the dependency counters and the fused cross-GPU exchange
 // follow lmce_bwd_kernel; every count covers both CTAs of a pair: each epilogue warp
-// publishes its rows of a GT tile (no CTA barrier: 16 counts per tile), each CTA its half of
-// a DXT tile, and a tile that read a G buffer releases it when its accumulator is full (the
-// UMMAs have read their operands by then). The pair leader (cluster rank 0) claims
-// tickets, checks dependencies and
-// hands each tile to both CTAs' schedule rings (the peer's through distributed shared
-// memory); only the leader issues UMMAs. Every wait is bounded.
+// publishes its rows of a GT tile (no CTA barrier: 16 counts per tile), each CTA its half
+// of a DXT tile, and a tile that read a G buffer releases it when its accumulator is full
+// (its UMMAs have read their operands by then). The pair leader (cluster rank 0) claims
+// tickets, checks dependencies and hands each tile to both CTAs' schedule rings (the
+// peer's through distributed shared memory); only the leader issues UMMAs. Every wait is
+// bounded.
 #pragma once
 
 #include "lmce_bwd.cuh"
