@@ -115,6 +115,17 @@ NVLS_MIN_DX_BYTES = 32 << 20  # fp32 dX size from which the fused exchange beats
 NVLS_MIN_WORLD = 8  # group size from which it wins at any size
 
 
+def wants_fused_exchange(n: int, h: int, world: int, mode: str = "auto") -> bool:
+    """Whether the dX sum of n tokens x h columns over `world` ranks should be fused into the
+    backward (before checking that the GPUs support it): LMCE_NVLS mode "0" never, "1" always,
+    otherwise from NVLS_MIN_DX_BYTES of fp32 dX or from NVLS_MIN_WORLD ranks."""
+    if mode == "0":
+        return False
+    if mode == "1":
+        return True
+    return 4 * n * h >= NVLS_MIN_DX_BYTES or world >= NVLS_MIN_WORLD
+
+
 def nvls_dx_exchange(n: int, h: int, dtype: torch.dtype, device: torch.device, group=None):
     """The group's ``NvlsDxExchange`` for n tokens, or None when the fused exchange is not
     used: LMCE_NVLS=0, or (default) fp32 dX below NVLS_MIN_DX_BYTES in a group of fewer than
@@ -123,10 +134,8 @@ def nvls_dx_exchange(n: int, h: int, dtype: torch.dtype, device: torch.device, g
     whenever the GPUs support it. One buffer per (device, group, h, dtype), reused for any n
     up to its capacity and replaced by one 1.5x larger when n outgrows it (every rank sees
     the same n, so all ranks reallocate together)."""
-    mode = os.environ.get("LMCE_NVLS", "auto")
-    if mode == "0" or device.type != "cuda":
-        return None
-    if mode != "1" and 4 * n * h < NVLS_MIN_DX_BYTES and dist.get_world_size(group) < NVLS_MIN_WORLD:
+    if device.type != "cuda" or not wants_fused_exchange(n, h, dist.get_world_size(group),
+                                                          os.environ.get("LMCE_NVLS", "auto")):
         return None
     key = (device.index, _group_name(group), h, dtype)
     cached = _NVLS_CACHE.get(key, False)

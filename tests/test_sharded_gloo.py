@@ -151,3 +151,22 @@ def test_exchange_capacity_grows_geometrically():
     # flag words of (row block m, rank, column tile) do not depend on N: a smaller call's flags
     # are the leading words of a larger allocation's
     assert NvlsDxExchange.flag_bytes(300, 1536, 8) <= NvlsDxExchange.flag_bytes(2048, 1536, 8)
+
+
+def test_fused_exchange_rule():
+    """When the vocab-sharded backward sums dX inside its kernel (NVLink SHARP) rather than with
+    an NCCL all-reduce afterwards: from 32 MiB of fp32 dX, or in groups of 8 GPUs at any size
+    (measured on B200: at 2048 tokens, H = 1536, the fused sum wins at 8 GPUs and ties at 2 and 4);
+    LMCE_NVLS=0 / 1 override it."""
+    from rus_b200.sharded import NVLS_MIN_DX_BYTES, wants_fused_exchange
+
+    assert NVLS_MIN_DX_BYTES == 32 << 20
+    small, large = (2048, 1536), (9434, 3584)  # 12.6 MB and 135 MB of fp32 dX
+    assert not wants_fused_exchange(*small, world=2)
+    assert not wants_fused_exchange(*small, world=4)
+    assert wants_fused_exchange(*small, world=8)
+    assert all(wants_fused_exchange(*large, world=w) for w in (2, 4, 8))
+    assert wants_fused_exchange(8192, 1024, world=2)  # exactly 32 MiB
+    assert not wants_fused_exchange(8191, 1024, world=2)
+    assert wants_fused_exchange(*small, world=2, mode="1")
+    assert not wants_fused_exchange(*large, world=8, mode="0")
