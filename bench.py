@@ -291,15 +291,20 @@ def choose_peak(peaks: dict, clk: dict):
 
 # ------------------------------------------------------------------ CPU side
 
-def cpu_reference(cfg: str, iters: int, warmup: int, threads: int, budget_s: float = CPU_BUDGET_S):
+def cpu_reference(cfg: str, iters: int, warmup: int, threads: int, budget_s: float = CPU_BUDGET_S, inputs=None):
     """The reference eager formula on the host CPU over the config's step, or over its first
     tokens when `warmup + iters` whole steps would not fit `budget_s` (the per-token cost is
-    calibrated on a 128-token run first). Returns (tokens/s per timed iteration, seconds per
-    iteration, tokens timed per iteration, tokens of the whole step)."""
+    calibrated on a 128-token run first). `inputs` = (X, labels, W) host tensors to use instead
+    of building the config on the host (the GPU arm passes its own, so that the outputs can be
+    compared). Returns (tokens/s per timed iteration, seconds per iteration, tokens timed per
+    iteration, tokens of the whole step, the last iteration's outputs)."""
     from oracle import lmce_oracle as orc
 
     torch.set_num_threads(threads)
-    X, y, W, _ = make_config(cfg, "cpu")
+    if inputs is None:
+        X, y, W, _ = make_config(cfg, "cpu")
+    else:
+        X, y, W = inputs
     n_full = int(y.numel())
     t0 = time.perf_counter()
     orc.eager_head(X[:128], y[:128], W, grads=True, grad_mode="eager")
@@ -308,13 +313,32 @@ def cpu_reference(cfg: str, iters: int, warmup: int, threads: int, budget_s: flo
     tokens = n_full if fit >= n_full else max(64, fit // 64 * 64)
     X, y = X[:tokens].contiguous(), y[:tokens].contiguous()
     times = []
+    out = None
     for i in range(warmup + iters):
         t0 = time.perf_counter()
-        orc.eager_head(X, y, W, grads=True, grad_mode="eager")
+        out = orc.eager_head(X, y, W, grads=True, grad_mode="eager")
         dt = time.perf_counter() - t0
         if i >= warmup:
             times.append(dt)
-    return [tokens / t for t in times], times, tokens, n_full
+    return [tokens / t for t in times], times, tokens, n_full, out
+
+
+def output_check(loss, nll, ent, arg, ref) -> dict:
+    """The GPU head's forward outputs against the eager reference formula's on the same inputs
+    (the host CPU's GEMM): `ok` = loss within 1e-3 relative and every token's nll within
+    1e-3 * max(|nll|, 1), the parity tests' bars. Entropy and argmax are reported, not gated: where
+    the two GEMMs round a row's top logits one fp16 ulp apart (config 5 plants exact top-2 ties
+    at logits near 40, where an ulp is 0.03), that row's entropy moves by up to ln 2 and its
+    argmax may flip; the GPU parity tests classify those rows against fp32 logits."""
+    nll, ent, arg = nll.detach().float().cpu(), ent.detach().float().cpu(), arg.detach().cpu()
+    rl, rn, re_, ra = float(ref["loss"]), ref["nll"].float(), ref["entropy"].float(), ref["argmax"]
+    loss_rel = abs(float(loss) - rl) / max(abs(rl), 1e-30)
+    nll_excess = float(((nll - rn).abs() / rn.abs().clamp(min=1.0)).max())
+    ent_excess = float(((ent - re_).abs() / re_.abs().clamp(min=1.0)).max())
+    agree = float((arg == ra).float().mean())
+    return {"loss": float(loss), "loss_oracle": rl, "loss_rel_diff": loss_rel, "nll_max_rel_diff": nll_excess,
+            "entropy_max_rel_diff": ent_excess, "argmax_agreement": agree,
+            "ok": loss_rel <= 1e-3 and nll_excess <= 1e-3}
 
 
 def run_reference_arm(args, rank, world):
@@ -322,7 +346,7 @@ def run_reference_arm(args, rank, world):
         return
     threads = os.cpu_count() or 1
     steps, warm = max(args.steps, 1), max(args.warmup, 1)
-    tps, times, tokens, n_full = cpu_reference(args.config, steps, warm, threads)
+    tps, times, tokens, n_full, _ = cpu_reference(args.config, steps, warm, threads)
     value = statistics.median(tps)
     H, V, dt, _ = CONFIGS[args.config]
     sample = ("the whole step" if tokens == n_full else f"the first {tokens} of the step's {n_full} tokens")
@@ -619,14 +643,24 @@ def main():
         print(f"device error word {err} on rank {rank}", file=sys.stderr)
 
     cpu_base = None
+    output_ok = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
         iters = 3
-        tps, _, tokens, n_full = cpu_reference(args.config, iters, 1, threads, budget_s=60.0)
+        # the same inputs the GPU arm timed (copied to the host), so that the outputs compare
+        tps, _, tokens, n_full, ref = cpu_reference(args.config, iters, 1, threads, budget_s=60.0,
+                                                    inputs=(Xh, yh, W.detach().cpu()))
         sample = "the whole step" if tokens == n_full else f"the first {tokens} of the step's {n_full} tokens"
         cpu_base = {"value": statistics.median(tps), "unit": "tokens/s", "cores": threads, "kind": "port",
                     "sample": f"{sample}, fwd+bwd, eager reference formula on the host CPU "
                               f"(median of {iters} after 1 warm-up)"}
+        if tokens == n_full:
+            # one more forward through the head on the timed inputs (after the timed region)
+            with torch.no_grad():
+                outs = head(Xg.detach(), y)
+            output_ok = output_check(*outs, ref)
+            if not output_ok["ok"]:
+                print(f"output check failed: {output_ok}", file=sys.stderr)
 
     if rank == 0:
         line = {
@@ -688,6 +722,8 @@ def main():
             line["per_rank"] = per_rank
         if cpu_base is not None:
             line["cpu_baseline"] = cpu_base
+        if output_ok is not None:
+            line["output_check"] = output_ok
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

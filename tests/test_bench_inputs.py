@@ -78,3 +78,26 @@ def test_clock_sampler_child_process(tmp_path, monkeypatch):
     assert a["sm_mhz"] == 1900.0 and a["reasons"] == ["sw_power_cap"] and a["power_capped_fraction"] == 1.0
     assert b["sm_mhz"] == 1800.0 and b["reasons"] == [] and b["sm_max_mhz"] == 1965.0
     assert bench.ClockSampler([]).summary()["samples"] == 0
+
+
+def test_output_check_gates_loss_and_nll():
+    """The bench compares its head's outputs on the timed inputs with the eager reference formula
+    (host CPU): loss and per-token nll gate `ok` at the parity tests' 1e-3; entropy and argmax
+    are reported only."""
+    from oracle import lmce_oracle as orc
+
+    g = torch.Generator().manual_seed(0)
+    X = torch.randn(64, 128, generator=g).half()
+    W = (torch.randn(500, 128, generator=g) * 0.02).half()
+    y = torch.randint(0, 500, (64,), generator=g)
+    y[:5] = -100
+    ref = orc.eager_head(X, y, W, grads=False)
+    same = bench.output_check(ref["loss"], ref["nll"], ref["entropy"], ref["argmax"], ref)
+    assert same["ok"] and same["loss_rel_diff"] == 0.0 and same["argmax_agreement"] == 1.0
+    assert not bench.output_check(ref["loss"] * 1.01, ref["nll"], ref["entropy"], ref["argmax"], ref)["ok"]
+    nll = ref["nll"].clone()
+    nll[7] += 0.01 * max(float(nll[7]), 1.0)
+    assert not bench.output_check(ref["loss"], nll, ref["entropy"], ref["argmax"], ref)["ok"]
+    ent = ref["entropy"] + 0.5  # reported, not gated
+    out = bench.output_check(ref["loss"], ref["nll"], ent, ref["argmax"], ref)
+    assert out["ok"] and out["entropy_max_rel_diff"] > 0.05
